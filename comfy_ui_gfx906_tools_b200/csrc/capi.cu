@@ -1,0 +1,235 @@
+// C ABI of the library (declared in include/gfx906_b200.h): argument checks
+// mirroring the reference binding (nodes/ComfyUI-Gfx906Int4/csrc/binding.cpp),
+// per-device caches, TMA descriptor encoding, dispatch to the kernels.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gfx {
+
+static thread_local char t_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return GFX_OK;
+}
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(GFX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(GFX_ERR_INVALID, "TMA base address %p is not 16-byte aligned", base);
+  if (row_stride_bytes % 16 != 0)
+    return set_error(GFX_ERR_INVALID, "TMA row stride %llu bytes is not a multiple of 16",
+                     (unsigned long long)row_stride_bytes);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(GFX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, box %u x %u", (int)r,
+                     (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+  return GFX_OK;
+}
+
+static bool valid_dtype(int d) { return d == GFX_DTYPE_F32 || d == GFX_DTYPE_F16 || d == GFX_DTYPE_BF16; }
+
+static int check_gemm_common(const char* fn, const void* x, int x_dtype, const void* w, const void* ws,
+                             int scale_dtype, void* y, int out_dtype, int M, int N, int K, int splits) {
+  if (M < 0 || N <= 0 || K <= 0)
+    return set_error(GFX_ERR_INVALID, "%s: expected M >= 0, N > 0, K > 0; got M=%d N=%d K=%d", fn, M, N, K);
+  if (K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "%s: expected K %% 32 == 0 (one scale per 32 elements), got K=%d", fn, K);
+  if (!valid_dtype(out_dtype))
+    return set_error(GFX_ERR_INVALID, "%s: unsupported out dtype code %d, expected 0 (f32) / 1 (f16) / 2 (bf16)", fn,
+                     out_dtype);
+  if (x_dtype != GFX_DTYPE_BF16)
+    return set_error(GFX_ERR_UNSUPPORTED, "%s: activations must be bfloat16 (dtype code 2), got code %d", fn, x_dtype);
+  if (scale_dtype != GFX_SCALE_F32 && scale_dtype != GFX_SCALE_F16)
+    return set_error(GFX_ERR_INVALID, "%s: scale dtype must be 0 (f32) or 1 (f16), got %d", fn, scale_dtype);
+  if (splits < 0 || splits > kMaxSplits)
+    return set_error(GFX_ERR_INVALID, "%s: splits must be in [0, %d], got %d", fn, kMaxSplits, splits);
+  if (M > 0 && (!x || !w || !ws || !y))
+    return set_error(GFX_ERR_INVALID, "%s: null pointer among x=%p w=%p scale=%p y=%p", fn, x, w, ws, y);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return set_error(GFX_ERR_INVALID, "%s: x (%p) and weights (%p) must be 16-byte aligned", fn, x, w);
+  if (scale_dtype == GFX_SCALE_F16 && (K % 64 != 0 || (reinterpret_cast<uintptr_t>(ws) & 3)))
+    return set_error(GFX_ERR_UNSUPPORTED, "%s: float16 scales need K %% 64 == 0 and 4-byte alignment (K=%d)", fn, K);
+  if (scale_dtype == GFX_SCALE_F32 && (reinterpret_cast<uintptr_t>(ws) & 3))
+    return set_error(GFX_ERR_INVALID, "%s: float32 scales must be 4-byte aligned", fn);
+  return GFX_OK;
+}
+
+}  // namespace gfx
+
+using namespace gfx;
+
+extern "C" {
+
+const char* gfx_last_error(void) { return t_last_error; }
+
+int gfx_version(void) { return 100; }
+
+int gfx_device_status(int clear) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return -set_error(GFX_ERR_CUDA, "gfx_device_status: %s", cudaGetErrorString(e));
+  const int parts[2] = {splitk_device_status(clear), tc_device_status(clear)};
+  for (int p : parts) {
+    if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
+    if (p && !v) v = p;
+  }
+  return v;
+}
+
+size_t w4a16_workspace_bytes(int M, int N, int K, int splits) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int sms = sm_count(current_device());
+  if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 0;
+  return splitk_workspace_bytes(M, N, K, splits, sms);
+}
+
+int w4a16_auto_splits(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 1;
+  if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 1;
+  return splitk_auto_splits(M, N, K, sm_count(current_device()));
+}
+
+int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype, const void* bias,
+               void* y, int out_dtype, int M, int N, int K, int splits, void* workspace, size_t workspace_bytes,
+               gfx_stream_t stream) {
+  int rc = check_gemm_common("w4a16_gemm", x, x_dtype, w_q4, w_scale, scale_dtype, y, out_dtype, M, N, K, splits);
+  if (rc) return rc;
+  if (M == 0) return GFX_OK;
+  const int sms = sm_count(current_device());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (splits == 0 && w4a16_tc_supported(M, N, K, scale_dtype))
+    return launch_w4a16_tc(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, st, sms);
+  return launch_w4a16_splitk(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, workspace,
+                             workspace_bytes, st, sms);
+}
+
+int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,
+               const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+               size_t workspace_bytes, gfx_stream_t stream) {
+  (void)x; (void)x_dtype; (void)w_q8; (void)w_scale; (void)scale_per_channel; (void)bias; (void)y;
+  (void)out_dtype; (void)M; (void)N; (void)K; (void)splits; (void)workspace; (void)workspace_bytes; (void)stream;
+  return set_error(GFX_ERR_UNSUPPORTED, "w8a16_gemm: not built yet");
+}
+
+size_t w8a16_workspace_bytes(int M, int N, int K, int splits) {
+  (void)M; (void)N; (void)K; (void)splits;
+  return 0;
+}
+
+int quantize_pack_int4(const void* x, int x_dtype, void* packed, float* scale, int64_t rows, int K, int div_mode,
+                       gfx_stream_t stream) {
+  if (rows < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "quantize_pack_int4: x must be [rows, K] with K %% 32 == 0, got [%lld, %d]",
+                     (long long)rows, K);
+  if (!valid_dtype(x_dtype)) return set_error(GFX_ERR_INVALID, "quantize_pack_int4: bad x dtype code %d", x_dtype);
+  if (div_mode != 0 && div_mode != 1)
+    return set_error(GFX_ERR_INVALID, "quantize_pack_int4: div_mode must be 0 or 1, got %d", div_mode);
+  if (rows == 0) return GFX_OK;
+  if (!x || !packed || !scale) return set_error(GFX_ERR_INVALID, "quantize_pack_int4: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 15))
+    return set_error(GFX_ERR_INVALID, "quantize_pack_int4: packed output must be 16-byte aligned");
+  return launch_quantize_pack_int4(x, x_dtype, packed, scale, rows, K, div_mode,
+                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int quantize_int8(const void* x, int x_dtype, void* q, float* scale, int64_t rows, int K, gfx_stream_t stream) {
+  if (rows < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "quantize_int8: x must be [rows, K] with K %% 32 == 0, got [%lld, %d]",
+                     (long long)rows, K);
+  if (!valid_dtype(x_dtype)) return set_error(GFX_ERR_INVALID, "quantize_int8: bad x dtype code %d", x_dtype);
+  if (rows == 0) return GFX_OK;
+  if (!x || !q || !scale) return set_error(GFX_ERR_INVALID, "quantize_int8: null pointer");
+  if ((reinterpret_cast<uintptr_t>(q) & 15))
+    return set_error(GFX_ERR_INVALID, "quantize_int8: q output must be 16-byte aligned");
+  return launch_quantize_int8(x, x_dtype, q, scale, rows, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, int N, int K, gfx_stream_t stream) {
+  if (N < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "repack_q4_0: expected N >= 0 and K %% 32 == 0, got N=%d K=%d", N, K);
+  if (N == 0) return GFX_OK;
+  if (!raw || !packed) return set_error(GFX_ERR_INVALID, "repack_q4_0: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 15) || (reinterpret_cast<uintptr_t>(raw) & 1))
+    return set_error(GFX_ERR_INVALID, "repack_q4_0: packed must be 16-byte and raw 2-byte aligned");
+  return launch_repack_q4_0(raw, packed, scale, scale_f16, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int int4_dequant(const void* w_q4, const void* w_scale, int scale_dtype, void* out, int out_dtype, int N, int K,
+                 gfx_stream_t stream) {
+  if (N < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "int4_dequant: expected N >= 0 and K %% 32 == 0, got N=%d K=%d", N, K);
+  if (!valid_dtype(out_dtype)) return set_error(GFX_ERR_INVALID, "int4_dequant: bad out dtype code %d", out_dtype);
+  if (scale_dtype != GFX_SCALE_F32 && scale_dtype != GFX_SCALE_F16)
+    return set_error(GFX_ERR_INVALID, "int4_dequant: scale dtype must be 0 or 1, got %d", scale_dtype);
+  if (N == 0) return GFX_OK;
+  if (!w_q4 || !w_scale || !out) return set_error(GFX_ERR_INVALID, "int4_dequant: null pointer");
+  if ((reinterpret_cast<uintptr_t>(w_q4) & 3) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return set_error(GFX_ERR_INVALID, "int4_dequant: weights must be 4-byte and out 16-byte aligned");
+  return launch_int4_dequant(w_q4, w_scale, scale_dtype, out, out_dtype, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int scales_to_f16(const float* scale, void* scale_f16, int64_t n, int* inexact, gfx_stream_t stream) {
+  if (n < 0 || !inexact || (n > 0 && (!scale || !scale_f16)))
+    return set_error(GFX_ERR_INVALID, "scales_to_f16: bad arguments");
+  return launch_scales_to_f16(scale, scale_f16, n, inexact, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,205 @@
+// Shared device/host helpers for the sm_100a int4/int8 weight-only GEMM library.
+//
+// Everything here is plain CUDA + inline PTX for sm_100a: mbarrier pipelines,
+// TMA (cp.async.bulk.tensor) loads, Ampere-style cp.async with mbarrier
+// completion, and the bounded waits every spin loop in this library uses.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "gfx906_b200.h"
+
+namespace gfx {
+
+// ---------------------------------------------------------------------------
+// device-side error word: bounded waits that give up record a code here
+// instead of hanging the GPU. Without relocatable device code every
+// translation unit has its own copy; each kernel file exports a host reader
+// (GFX_DEFINE_STATUS_READER) and gfx_device_status combines them.
+// ---------------------------------------------------------------------------
+static __device__ int g_device_error = 0;
+
+#define GFX_DEFINE_STATUS_READER(name)                                        \
+  int name(int clear) {                                                       \
+    int v = 0;                                                                \
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) \
+      return -1;                                                              \
+    if (clear && v) {                                                         \
+      int zero = 0;                                                           \
+      cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));                 \
+    }                                                                         \
+    return v;                                                                 \
+  }
+
+// Wall-clock budget of one bounded wait (ns). A healthy pipeline completes
+// every wait in microseconds; this only ends waits that can never complete.
+constexpr unsigned long long kWaitTimeoutNs = 2000ull * 1000ull * 1000ull;
+
+enum DeviceErrorCode : int {
+  kDevErrNone = 0,
+  kDevErrFullBarrierTimeout = 1,
+  kDevErrEmptyBarrierTimeout = 2,
+  kDevErrMmaBarrierTimeout = 3,
+  kDevErrEpilogueBarrierTimeout = 4,
+};
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void record_device_error(int code) {
+  atomicCAS(&g_device_error, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory addresses and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+// Make barrier inits visible to the async proxy (TMA, tcgen05) and the cluster.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code`) once the timeout passes,
+// or at once if another thread of the grid already recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0u) {
+      if (*(volatile int*)&g_device_error != 0) return false;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        record_device_error(code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor) and Ampere-style cp.async
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled TMA load, completion counted on `bar` in bytes. c0 is the
+// innermost coordinate (elements); c0 * elem_size must be 16-byte aligned.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 4-byte async copy global -> shared; src_bytes = 0 zero-fills (no read).
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// The mbarrier receives one arrival when all of this thread's prior cp.async
+// copies have landed (the barrier's expected count must include it).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// global loads / misc
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// d = (a & b) ^ c in one LOP3.
+__device__ __forceinline__ uint32_t and_xor(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+}  // namespace gfx
+
+// ---------------------------------------------------------------------------
+// host side helpers (defined in capi.cu)
+// ---------------------------------------------------------------------------
+namespace gfx {
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int sm_count(int device);
+int current_device();
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+}  // namespace gfx

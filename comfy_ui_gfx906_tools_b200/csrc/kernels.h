@@ -1,0 +1,40 @@
+// Internal launcher declarations shared by the C-ABI layer (capi.cu) and the
+// kernel translation units. Not part of the public ABI (include/gfx906_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gfx {
+
+constexpr int kMaxSplits = 16;
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// W4A16, small M (split-K, mma.sync register dequant) -- w4a16_splitk.cu
+int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+                        int out_dtype, int M, int N, int K, int splits, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream, int sms);
+size_t splitk_workspace_bytes(int M, int N, int K, int splits, int sms);
+int splitk_auto_splits(int M, int N, int K, int sms);
+int splitk_device_status(int clear);
+
+// W4A16, large M (tcgen05 + TMEM, persistent) -- w4a16_tc.cu
+int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
+bool w4a16_tc_supported(int M, int N, int K, int scale_dtype);
+int tc_device_status(int clear);
+
+// loaders / helpers -- pack.cu
+int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
+                        cudaStream_t stream);
+int launch_repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, int N, int K,
+                       cudaStream_t stream);
+int launch_quantize_pack_int4(const void* x, int x_dtype, void* packed, float* scale, int64_t rows, int K,
+                              int div_mode, cudaStream_t stream);
+int launch_quantize_int8(const void* x, int x_dtype, void* q, float* scale, int64_t rows, int K,
+                         cudaStream_t stream);
+int launch_scales_to_f16(const float* s, void* s16, int64_t n, int* inexact, cudaStream_t stream);
+
+}  // namespace gfx

@@ -1,0 +1,387 @@
+"""Operator layer: the reference's Python-facing int4 surface, on sm_100a.
+
+Mirrors ``nodes/ComfyUI-Gfx906Int4/ops.py`` of luna-niemitalo/comfy_ui_gfx906_tools
+(same names, argument order, buffers, packed layout and scale format) with the
+compute routed through this package's C-ABI library (``_lib``):
+
+  * ``int4_linear`` (ops.py:167-183) -> ``gemm_w4a16``: bf16 activations
+    against the packed int4 weights, fp32 accumulation (weight-only; the
+    reference quantizes activations to int4 as well, see DESIGN notes in the
+    package docstring of ``gemm_int4``);
+  * ``quantize_pack_int4`` (ops.py:108-126) and ``repack_q4_0_native``
+    (ops.py:129-164) run as GPU kernels with results identical to the
+    reference's torch code on the tensor's own device (CPU tensors: the
+    IEEE-division semantics of torch on CPU; CUDA tensors: the reciprocal
+    multiply torch uses for ``tensor / 7.0`` on CUDA);
+  * ``Gfx906Int4Ops.Linear`` (ops.py:199-260) with the same buffers
+    ``weight_q4`` int8 [N, K/2] / ``weight_scale`` fp32 [N, K/32], the same
+    ``quantized`` rule and quantize-on-load.
+
+There is no CPU fallback: a CUDA build of the library is required for every
+compute entry point.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+BLOCK = 32
+ROTATION_SEED = 0
+
+_DTYPE_CODE = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise RuntimeError(f"unsupported dtype {dt}, expected float32/float16/bfloat16") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be on a CUDA device, got {t.device}")
+
+
+# ---------------------------------------------------------------------------
+# per-(device, stream) split-K workspace; zero-filled once, the kernel leaves
+# its counters at zero after every call
+# ---------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    key = (device.index, stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+# ---------------------------------------------------------------------------
+# Hadamard rotation helpers (reference ops.py:43-105), torch on the tensor's device
+# ---------------------------------------------------------------------------
+_HADAMARD_CACHE = {}
+_ROTATION_CACHE = {}
+
+
+def _hadamard(n: int, device, dtype=torch.float32):
+    """Orthonormal Sylvester Hadamard matrix of order n (a power of two)."""
+    key = (n, str(device), dtype)
+    if key not in _HADAMARD_CACHE:
+        if n & (n - 1) != 0:
+            raise AssertionError(f"Hadamard order {n} must be a power of two")
+        h = torch.ones(1, 1, device=device, dtype=dtype)
+        while h.shape[0] < n:
+            h = torch.cat([torch.cat([h, h], dim=1), torch.cat([h, -h], dim=1)], dim=0)
+        _HADAMARD_CACHE[key] = h / (n ** 0.5)
+    return _HADAMARD_CACHE[key]
+
+
+def choose_rotation_group(in_features: int, max_group: int = 128, min_group: int = 32) -> int | None:
+    """Largest power-of-two group <= max_group dividing in_features, or None
+    below min_group (ops.py:54-65)."""
+    g = max_group
+    while g >= min_group:
+        if in_features % g == 0:
+            return g
+        g //= 2
+    return None
+
+
+def get_group_rotation(in_features: int, group: int, device) -> torch.Tensor:
+    """R = H_group * diag(random signs), signs from a CPU generator seeded
+    ROTATION_SEED ^ group (ops.py:68-82), so folding time and forward time agree."""
+    key = (in_features, group, str(device))
+    if key not in _ROTATION_CACHE:
+        g = torch.Generator(device="cpu").manual_seed(ROTATION_SEED ^ group)
+        signs = (torch.randint(0, 2, (group,), generator=g).float() * 2 - 1).to(device)
+        _ROTATION_CACHE[key] = _hadamard(group, device) * signs
+    return _ROTATION_CACHE[key]
+
+
+def apply_group_rotation(t: torch.Tensor, R: torch.Tensor, group: int) -> torch.Tensor:
+    """Rotate every group-sized chunk of the last dim: flat @ R^T (ops.py:85-105)."""
+    shape = t.shape
+    flat = t.reshape(-1, group)
+    if flat.device.type == "cpu" and torch.cuda.is_available():
+        rotated = (flat.cuda() @ R.t().cuda()).to("cpu")
+    else:
+        rotated = flat @ R.t().to(flat.device)
+    return rotated.reshape(shape)
+
+
+# ---------------------------------------------------------------------------
+# packing / loader kernels
+# ---------------------------------------------------------------------------
+def quantize_pack_int4(t: torch.Tensor, block: int = BLOCK):
+    """t [..., K] float -> (packed int8 [..., K/2], scale float32 [..., K/block]).
+
+    Same result as the reference (ops.py:108-126) evaluated on t's device:
+    a CPU tensor is quantized with torch-CPU semantics (IEEE ``amax / 7``),
+    a CUDA tensor with torch-CUDA semantics (``amax * (1/7)``). The work runs
+    on the GPU either way; CPU tensors are staged through the current device.
+    """
+    if block != BLOCK:
+        raise RuntimeError(f"block must be {BLOCK}, got {block}")
+    shape = t.shape
+    K = shape[-1]
+    if K % block != 0:
+        raise AssertionError(f"last dim {K} not divisible by block {block}")
+    on_cpu = not t.is_cuda
+    if on_cpu and not torch.cuda.is_available():
+        raise RuntimeError("quantize_pack_int4 needs a CUDA device (the packing runs as a GPU kernel)")
+    dev = torch.device("cuda", torch.cuda.current_device()) if on_cpu else t.device
+    src = t.reshape(-1, K)
+    if src.dtype not in _DTYPE_CODE:
+        src = src.float()
+    src = src.to(dev).contiguous()
+    rows = src.shape[0]
+    packed = torch.empty(rows, K // 2, dtype=torch.int8, device=dev)
+    scale = torch.empty(rows, K // block, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("quantize_pack_int4", src.data_ptr(), _dtype_code(src.dtype), packed.data_ptr(), scale.data_ptr(),
+                  rows, K, 0 if on_cpu else 1, _stream(dev))
+    packed = packed.reshape(*shape[:-1], K // 2)
+    scale = scale.reshape(*shape[:-1], K // block)
+    if on_cpu:
+        packed, scale = packed.cpu(), scale.cpu()
+    return packed, scale
+
+
+def repack_q4_0_native(raw_bytes: torch.Tensor, out_features: int, in_features: int, block: int = BLOCK):
+    """Lossless ggml Q4_0 -> native repack (ops.py:129-164), as a GPU kernel.
+    Returns tensors on raw_bytes' device."""
+    if block != BLOCK:
+        raise RuntimeError(f"block must be {BLOCK}, got {block}")
+    nbytes = out_features * (in_features // block) * 18
+    raw = raw_bytes.reshape(-1).view(torch.uint8)
+    if raw.numel() != nbytes:
+        raise RuntimeError(f"expected {nbytes} Q4_0 bytes for [{out_features}, {in_features}], got {raw.numel()}")
+    on_cpu = not raw.is_cuda
+    dev = torch.device("cuda", torch.cuda.current_device()) if on_cpu else raw.device
+    raw = raw.to(dev).contiguous()
+    packed = torch.empty(out_features, in_features // 2, dtype=torch.int8, device=dev)
+    scale = torch.empty(out_features, in_features // block, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("repack_q4_0", raw.data_ptr(), packed.data_ptr(), scale.data_ptr(), None, out_features,
+                  in_features, _stream(dev))
+    if on_cpu:
+        packed, scale = packed.cpu(), scale.cpu()
+    return packed, scale
+
+
+def dequantize_int4(w_packed: torch.Tensor, w_scale: torch.Tensor, out_dtype: torch.dtype = torch.float32):
+    """Dequantize native int4 weights on the GPU: code * scale as one fp32
+    multiply, rounded once to out_dtype (int4_train_test.py:46-52; bf16 out
+    = nodes.py:51-52 for a bf16 model)."""
+    _require_cuda(w_packed, "w_packed")
+    N, half_k = w_packed.shape
+    K = half_k * 2
+    scale_code = _lib.SCALE_F16 if w_scale.dtype == torch.float16 else _lib.SCALE_F32
+    if w_scale.dtype not in (torch.float16, torch.float32):
+        raise RuntimeError(f"scales must be float32 or float16, got {w_scale.dtype}")
+    wp, ws = w_packed.contiguous(), w_scale.contiguous()
+    out = torch.empty(N, K, dtype=out_dtype, device=w_packed.device)
+    with torch.cuda.device(w_packed.device):
+        _lib.call("int4_dequant", wp.data_ptr(), ws.data_ptr(), scale_code, out.data_ptr(), _dtype_code(out_dtype), N,
+                  K, _stream(w_packed.device))
+    return out
+
+
+def scales_to_f16_if_exact(w_scale: torch.Tensor):
+    """fp16 copy of fp32 scales when every value survives the round trip
+    exactly (true for Q4_0-sourced weights), else None."""
+    _require_cuda(w_scale, "w_scale")
+    s = w_scale.contiguous().float()
+    out = torch.empty(s.shape, dtype=torch.float16, device=s.device)
+    bad = torch.empty(1, dtype=torch.int32, device=s.device)
+    with torch.cuda.device(s.device):
+        _lib.call("scales_to_f16", s.data_ptr(), out.data_ptr(), s.numel(), bad.data_ptr(), _stream(s.device))
+    return out if int(bad.item()) == 0 else None
+
+
+# ---------------------------------------------------------------------------
+# GEMM entry points
+# ---------------------------------------------------------------------------
+def gemm_int4_auto_splits(M: int, N: int, K: int) -> int:
+    """Split-K count the W4A16 GEMM picks for [M, K] x [N, K]^T on the current
+    device (the counterpart of gemm_int4_auto_splits, binding.cpp:358-361)."""
+    return int(_lib.load().w4a16_auto_splits(int(M), int(N), int(K)))
+
+
+def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, bias: torch.Tensor | None,
+               out_dtype: torch.dtype, splits: int = 0) -> torch.Tensor:
+    """C[M, N] = x[M, K] @ dequant(B_packed, B_scale)^T (+ bias), fp32 accumulate.
+
+    x: bf16 [M, K] (other float dtypes are converted to bf16 first).
+    B_packed int8 [N, K/2]; B_scale float32 (reference format) or float16
+    [N, K/32]; bias [N] in out_dtype or None. Argument checks and messages
+    follow gemm_int4 (binding.cpp:76-101).
+    """
+    if not (x.is_cuda and B_packed.is_cuda):
+        raise RuntimeError("inputs must be on device")
+    if x.device != B_packed.device:
+        raise RuntimeError("x and B must be on the same device")
+    if B_packed.dtype != torch.int8:
+        raise RuntimeError(f"packed weights must be int8, got {B_packed.dtype}")
+    if x.dim() != 2 or B_packed.dim() != 2 or x.shape[1] != B_packed.shape[1] * 2:
+        raise RuntimeError(f"expected x [M, K], B [N, K/2]; got x {tuple(x.shape)} B {tuple(B_packed.shape)}")
+    M, K = x.shape
+    N = B_packed.shape[0]
+    if K % 32 != 0:
+        raise RuntimeError(f"expected K % 32 == 0, got K={K}")
+    if B_scale.dtype not in (torch.float32, torch.float16):
+        raise RuntimeError(f"scales must be float32 (or float16), got {B_scale.dtype}")
+    if B_scale.numel() != N * (K // 32):
+        raise RuntimeError(f"scales must be [N, K/32] = {N * (K // 32)} elements, got {B_scale.numel()}")
+    if not (0 <= splits <= 16):
+        raise RuntimeError(f"splits must be in [0, 16], got {splits}")
+    out = torch.empty(M, N, dtype=out_dtype, device=x.device)
+    if M == 0:
+        return out
+    bias_ptr = None
+    if bias is not None:
+        if bias.dtype != out_dtype:
+            raise RuntimeError(f"bias dtype {bias.dtype} != out dtype {out_dtype}")
+        if bias.numel() != N:
+            raise RuntimeError(f"bias must have {N} elements, got {bias.numel()}")
+        bias = bias.contiguous()
+        bias_ptr = bias.data_ptr()
+    xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+    xb = xb.contiguous()
+    Bp, Bs = B_packed.contiguous(), B_scale.contiguous()
+    dev = x.device
+    with torch.cuda.device(dev):
+        stream = _stream(dev)
+        L = _lib.load()
+        nbytes = int(L.w4a16_workspace_bytes(M, N, K, splits))
+        ws = _workspace(dev, stream, nbytes)
+        _lib.call("w4a16_gemm", xb.data_ptr(), _lib.DTYPE_BF16, Bp.data_ptr(), Bs.data_ptr(),
+                  _lib.SCALE_F16 if Bs.dtype == torch.float16 else _lib.SCALE_F32, bias_ptr, out.data_ptr(),
+                  _dtype_code(out_dtype), M, N, K, splits, ws.data_ptr() if ws is not None else None,
+                  ws.numel() if ws is not None else 0, stream)
+    return out
+
+
+def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                rotation_group: int = 0) -> torch.Tensor:
+    """x [..., K] float, packed weights from quantize_pack_int4 (folded through
+    the same rotation when rotation_group != 0), bias in x.dtype or None ->
+    [..., N] in x.dtype (signature of ops.py:167)."""
+    shape = x.shape
+    K = shape[-1]
+    x2d = x.reshape(-1, K)
+    if rotation_group:
+        R = get_group_rotation(K, rotation_group, x2d.device)
+        x2d = apply_group_rotation(x2d.float(), R, rotation_group)
+    out = gemm_w4a16(x2d, w_packed, w_scale, bias, x.dtype)
+    return out.reshape(*shape[:-1], w_packed.shape[0])
+
+
+# ---------------------------------------------------------------------------
+# custom_operations integration (reference ops.py:186-276)
+# ---------------------------------------------------------------------------
+try:  # ComfyUI present: subclass its op set exactly like the reference
+    import comfy.ops as _comfy_ops  # type: ignore
+
+    _OpsBase = _comfy_ops.disable_weight_init
+except Exception:  # standalone use (tests, benches): a plain container class
+    class _OpsBase:  # noqa: D401 - stand-in for comfy.ops.disable_weight_init
+        """Stand-in base when ComfyUI is not importable."""
+
+
+class Gfx906Int4Ops(_OpsBase):
+    class Linear(torch.nn.Module):
+        def __init__(self, in_features, out_features, bias=True, device=None, dtype=None, rotation_group=0):
+            super().__init__()
+            self.in_features = in_features
+            self.out_features = out_features
+            self.rotation_group = rotation_group
+            # Layers narrower than one quant block stay float (ops.py:206-212).
+            self.quantized = in_features % BLOCK == 0 and in_features >= BLOCK
+            if self.quantized:
+                self.register_buffer("weight_q4", torch.empty(out_features, in_features // 2, dtype=torch.int8,
+                                                              device=device))
+                self.register_buffer("weight_scale", torch.empty(out_features, in_features // BLOCK,
+                                                                 dtype=torch.float32, device=device))
+            else:
+                self.weight = torch.nn.Parameter(torch.empty(out_features, in_features, device=device, dtype=dtype))
+            if bias:
+                self.bias = torch.nn.Parameter(torch.empty(out_features, device=device, dtype=dtype))
+            else:
+                self.register_parameter("bias", None)
+            self._scale_cache = None  # (device, version, ptr, fp16 copy or False)
+
+        quantize_device = None
+        quantized_on_load = 0
+
+        def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                  error_msgs):
+            key = prefix + "weight"
+            if self.quantized and self.quantize_device is not None and key in state_dict:
+                w = state_dict.pop(key)
+                if w.dtype not in (torch.float32, torch.float16, torch.bfloat16) or \
+                        tuple(w.shape) != (self.out_features, self.in_features):
+                    raise RuntimeError(f"{key}: expected a float [{self.out_features}, {self.in_features}] weight, "
+                                       f"got {w.dtype} {tuple(w.shape)}")
+                w_float = w.to(self.quantize_device).float()
+                if self.rotation_group:
+                    R = get_group_rotation(self.in_features, self.rotation_group, w_float.device)
+                    w_float = apply_group_rotation(w_float, R, self.rotation_group)
+                packed, scale = quantize_pack_int4(w_float, BLOCK)
+                state_dict[prefix + "weight_q4"] = packed.to(w.device)
+                state_dict[prefix + "weight_scale"] = scale.to(w.device)
+                type(self).quantized_on_load += 1
+            self._scale_cache = None
+            super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                          error_msgs)
+
+        def _device_scale(self, weight_scale: torch.Tensor) -> torch.Tensor:
+            """The scale buffer the kernel reads: an fp16 copy when every fp32
+            scale is exactly an fp16 value (halves scale traffic; identical
+            results), else the fp32 buffer itself. Cached per buffer version."""
+            key = (weight_scale.device, weight_scale._version, weight_scale.data_ptr())
+            c = self._scale_cache
+            if c is not None and c[0] == key:
+                return c[1] if c[1] is not None else weight_scale
+            s16 = scales_to_f16_if_exact(weight_scale) if self.in_features % 64 == 0 else None
+            self._scale_cache = (key, s16)
+            return s16 if s16 is not None else weight_scale
+
+        def forward(self, x):
+            if not self.quantized:
+                bias = self.bias.to(x.device, x.dtype) if self.bias is not None else None
+                return torch.nn.functional.linear(x, self.weight.to(x.device, x.dtype), bias)
+            weight_q4 = self.weight_q4.to(x.device)
+            weight_scale = self.weight_scale.to(x.device)
+            if weight_scale is self.weight_scale:
+                weight_scale = self._device_scale(weight_scale)
+            bias = self.bias.to(x.device, x.dtype) if self.bias is not None else None
+            return int4_linear(x, weight_q4, weight_scale, bias, self.rotation_group)
+
+
+def make_load_quantizing_ops(base_ops, quantize_device, rotate):
+    """custom_operations that quantize plain float Linear weights while the
+    state dict loads (ops.py:263-276)."""
+    class Linear(Gfx906Int4Ops.Linear):
+        quantized_on_load = 0
+
+        def __init__(self, in_features, out_features, bias=True, device=None, dtype=None):
+            group = (choose_rotation_group(in_features) or 0) if rotate else 0
+            super().__init__(in_features, out_features, bias, device, dtype, rotation_group=group)
+
+    Linear.quantize_device = torch.device(quantize_device)
+    return type("Gfx906Int4LoadOps", (base_ops,), {"Linear": Linear})

@@ -1,0 +1,142 @@
+/*
+ * gfx906_b200.h -- C ABI of the B200 (sm_100a) int4 / int8 weight-only linear
+ * library: the drop-in boundary under the reference's Python operator layer.
+ *
+ * Reference: luna-niemitalo/comfy_ui_gfx906_tools, nodes/ComfyUI-Gfx906Int4.
+ * Each entry point names the reference interface it replaces (path:line).
+ *
+ * Conventions
+ *  - All pointers are device pointers unless stated; the caller owns every
+ *    buffer (inputs, outputs, workspaces). The library never allocates or
+ *    frees caller memory.
+ *  - Work is enqueued on `stream` (a cudaStream_t) of the current device; the
+ *    caller makes the device that owns the buffers current first (the
+ *    reference binds a CUDAGuard for the same reason, binding.cpp:56-59).
+ *  - Return 0 on success, otherwise a GFX_ERR_* code; gfx_last_error() then
+ *    holds a message (thread-local) with expected vs actual values. Nothing
+ *    aborts the process.
+ *  - dtype codes follow the reference binding (binding.cpp:45-50):
+ *    0 = float32, 1 = float16, 2 = bfloat16.
+ *  - Packed int4 weight layout (ops.py:108-126, int4_gemm_scaled.hip:6-10):
+ *    int8 [N, K/2], two's-complement nibbles, element e of each 32-chunk is
+ *    nibble e%8 of little-endian 32-bit word e/8; scales [N, K/32].
+ */
+#ifndef GFX906_B200_H
+#define GFX906_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gfx_stream_t; /* == cudaStream_t */
+
+#define GFX_OK 0
+#define GFX_ERR_INVALID 1     /* bad argument (shape, dtype, null pointer)          */
+#define GFX_ERR_UNSUPPORTED 2 /* valid for the reference, not supported here (yet)  */
+#define GFX_ERR_WORKSPACE 3   /* workspace missing or smaller than required         */
+#define GFX_ERR_CUDA 4        /* CUDA runtime / launch error                        */
+#define GFX_ERR_DEVICE 5      /* a bounded device-side wait gave up (see status)    */
+
+#define GFX_DTYPE_F32 0
+#define GFX_DTYPE_F16 1
+#define GFX_DTYPE_BF16 2
+
+#define GFX_SCALE_F32 0 /* scales float32 [N, K/32] (the reference's format)      */
+#define GFX_SCALE_F16 1 /* scales float16 [N, K/32] (only when exactly fp16)      */
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* gfx_last_error(void);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int gfx_version(void);
+
+/* Device-side status word of the current device: 0 = healthy, else the code
+ * of the first bounded wait that gave up. Synchronises the device. clear != 0
+ * resets the word to 0. */
+int gfx_device_status(int clear);
+
+/*
+ * W4A16 GEMM:  y[M, N] = x[M, K] @ dequant(w_q4, w_scale)^T (+ bias)
+ *
+ * Replaces the int4 GEMM under Gfx906Int4Ops.Linear.forward -> int4_linear
+ * (ops.py:167-183 -> binding.cpp:73-112 gemm_int4 -> int4_gemm_scaled.hip
+ * int4_gemm_kernel), keeping the weight buffers, layout and scale format; the
+ * activation stays bf16 (weight-only), the accumulation is fp32.
+ *   x        bf16 [M, K] row-major (x_dtype must be GFX_DTYPE_BF16)
+ *   w_q4     int8 [N, K/2] packed as above;  K % 32 == 0
+ *   w_scale  [N, K/32], GFX_SCALE_F32 or GFX_SCALE_F16
+ *   bias     [N] in out_dtype, or NULL (binding.cpp:97: bias dtype == out dtype)
+ *   y        [M, N] in out_dtype
+ *   splits   split-K count, 0 = automatic (gemm_int4's `splits`, binding.cpp:101-105)
+ *   workspace / workspace_bytes: scratch for split-K partials, at least
+ *            w4a16_workspace_bytes(M, N, K, splits); must hold zeros before
+ *            its first use; every call leaves its counters at zero again.
+ * M == 0 is a no-op (binding.cpp:93).
+ */
+int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+               const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+               size_t workspace_bytes, gfx_stream_t stream);
+
+/* Scratch bytes w4a16_gemm needs for (M, N, K, splits) on the current device. */
+size_t w4a16_workspace_bytes(int M, int N, int K, int splits);
+
+/* Split-K count w4a16_gemm picks when splits == 0 (gemm_int4_auto_splits,
+ * binding.cpp:358-361 / auto_splits binding.cpp:36-43). */
+int w4a16_auto_splits(int M, int N, int K);
+
+/*
+ * W8A16 GEMM:  y = x @ dequant_int8(w_q8, w_scale)^T (+ bias)
+ * The int8 sibling of w4a16_gemm (gemm_int8, binding.cpp:190-217; weights
+ * from quantize_int8, binding.cpp:174-186).
+ *   w_q8     int8 [N, K]
+ *   w_scale  float32 [N, K/32] (block scales, the reference layout) when
+ *            scale_per_channel == 0; float16 [N] per-output-channel scale
+ *            when scale_per_channel == 1.
+ */
+int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,
+               const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+               size_t workspace_bytes, gfx_stream_t stream);
+
+size_t w8a16_workspace_bytes(int M, int N, int K, int splits);
+
+/*
+ * Block-32 int4 quantize + pack (ops.quantize_pack_int4, ops.py:108-126; the
+ * activation quantizer quantize_int4, binding.cpp:53-68 /
+ * int4_gemm_scaled.hip:197-220, is div_mode 1).
+ *   x       [rows, K] in x_dtype; K % 32 == 0
+ *   packed  int8 [rows, K/2];  scale float32 [rows, K/32]
+ *   div_mode 0: scale = amax / 7 as an IEEE division (torch on CPU);
+ *            1: scale = amax * (1/7) (torch on CUDA, and the HIP kernel).
+ */
+int quantize_pack_int4(const void* x, int x_dtype, void* packed, float* scale, int64_t rows, int K, int div_mode,
+                       gfx_stream_t stream);
+
+/* Block-32 int8 quantize (quantize_int8, binding.cpp:174-186 /
+ * int8_gemm.hip:217-246): q int8 [rows, K], scale float32 [rows, K/32]. */
+int quantize_int8(const void* x, int x_dtype, void* q, float* scale, int64_t rows, int K, gfx_stream_t stream);
+
+/* Lossless ggml Q4_0 -> native repack (ops.repack_q4_0_native, ops.py:129-164).
+ *   raw     N*(K/32)*18 bytes of Q4_0 blocks (2-byte fp16 d + 16 nibble bytes)
+ *   packed  int8 [N, K/2];  scale float32 [N, K/32];  scale_f16 float16 [N, K/32]
+ *           (either scale pointer may be NULL). */
+int repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, int N, int K, gfx_stream_t stream);
+
+/* Dequantize packed int4 weights: out[N, K] = code * scale, computed as one
+ * fp32 multiply and, for out_dtype bf16/f16, rounded to nearest-even once
+ * (int4_train_test.py:46-52; nodes.py:51-52). The bf16 output is the exact
+ * operand the W4A16 tensor-core kernel multiplies with. */
+int int4_dequant(const void* w_q4, const void* w_scale, int scale_dtype, void* out, int out_dtype, int N, int K,
+                 gfx_stream_t stream);
+
+/* Convert float32 scales to float16 and count the ones that did not survive
+ * the round trip exactly (*inexact, a device int, is overwritten). */
+int scales_to_f16(const float* scale, void* scale_f16, int64_t n, int* inexact, gfx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GFX906_B200_H */

@@ -1,0 +1,259 @@
+"""CPU restatement (numpy) of the reference's int4 / int8 weight path.
+
+TEST INFRASTRUCTURE ONLY: this module is the checker the GPU kernels are
+compared against and the CPU stand-in timed as the reference's CPU path. The
+product package never imports it.
+
+Pinning: every function below is checked against golden vectors that
+``tests/golden/make_golden.py`` produced by importing and running the
+reference's own Python (``nodes/ComfyUI-Gfx906Int4/ops.py`` with a one-class
+``comfy.ops`` stub, ``nodes.py`` with module stubs, and the harness helpers
+``develop/experiments/2026-10-11/int4_train_test.py:46-52`` /
+``develop/harness/bench_int8.py:32-33`` extracted verbatim). The reference's
+HIP quantizers (``int4_gemm_scaled.hip:197-220``, ``int8_gemm.hip:217-246``)
+cannot run here (gfx906 only); their restatements are pinned only through the
+torch-semantics twin they document (``quantize_pack_int4`` with a reciprocal
+divide), which is called out per function.
+
+Layouts (reference ``ops.py:108-126``, ``csrc/int4_gemm_scaled.hip:6-10``):
+  * native int4: int8 ``[N, K/2]``, two's-complement nibbles, interleaved:
+    byte j low nibble = element 2j, high nibble = element 2j+1, i.e. element
+    e of every 32-chunk is nibble e%8 of little-endian 32-bit word e/8;
+    scales fp32 ``[N, K/32]``.
+  * ggml Q4_0 (ingest, ``ops.py:129-164``): 18-byte blocks, fp16 ``d`` then
+    16 bytes of offset-8 nibbles in split-half order (byte i low = element i,
+    high = element i+16); value = (u - 8) * d.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+BLOCK = 32
+Q4_0_BLOCK_BYTES = 18
+
+__all__ = [
+    "BLOCK", "f32_to_bf16_bits", "bf16_bits_to_f32", "round_to_bf16", "f32_to_f16_bits",
+    "quantize_pack_int4", "repack_q4_0_native", "dequant_int4", "dequant_int4_bf16_bits",
+    "quantize_dequantize_int4", "build_q4_0_bytes", "w4a16_matmul", "quantize_int8",
+    "dequant_int8", "w8a16_matmul", "parity_metrics", "unpack_int4_codes", "pack_int4_codes",
+]
+
+
+# ---------------------------------------------------------------------------
+# float helpers
+# ---------------------------------------------------------------------------
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16, returned as uint16 bit patterns
+    (torch's ``Tensor.to(torch.bfloat16)`` rule for finite values)."""
+    b = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    rounded = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+    return rounded.astype(np.uint16)
+
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_to_bf16(a: np.ndarray) -> np.ndarray:
+    """fp32 values rounded to the nearest bf16 (RNE), returned as fp32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(a))
+
+
+def f32_to_f16_bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+# ---------------------------------------------------------------------------
+# int4 packing (reference ops.py:108-164)
+# ---------------------------------------------------------------------------
+def pack_int4_codes(codes: np.ndarray) -> np.ndarray:
+    """codes int [..., K] in [-8, 7] -> int8 [..., K/2], interleaved
+    two's-complement nibbles (ops.py:119-121)."""
+    c = np.asarray(codes).astype(np.int32)
+    lo = c[..., 0::2] & 0xF
+    hi = c[..., 1::2] & 0xF
+    return (lo | (hi << 4)).astype(np.uint8).view(np.int8)
+
+
+def unpack_int4_codes(packed: np.ndarray) -> np.ndarray:
+    """int8 [..., K/2] -> int32 codes [..., K] in [-8, 7]; the exact inverse of
+    ``pack_int4_codes`` (int4_train_test.py:46-51 reads the same layout as
+    nibble e%8 of word e/8)."""
+    p = np.ascontiguousarray(packed).view(np.uint8).astype(np.int32)
+    nib = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.int32)
+    nib[..., 0::2] = p & 0xF
+    nib[..., 1::2] = (p >> 4) & 0xF
+    return np.where(nib > 7, nib - 16, nib)
+
+
+def quantize_pack_int4(t: np.ndarray, block: int = BLOCK, div_mode: str = "true"):
+    """Reference ``ops.quantize_pack_int4`` (ops.py:108-126).
+
+    t: float array [..., K] (already float32-representable: fp32, or fp16 /
+    bf16 values widened exactly, as ``.float()`` does at ops.py:114).
+    Returns (packed int8 [..., K/2], scale float32 [..., K/block]).
+
+    div_mode selects how ``amax / 7.0`` is evaluated:
+      "true"  -- an IEEE fp32 division: torch's CPU kernel (checked against
+                 the reference run on CPU in the golden fixtures);
+      "recip" -- ``amax * (1/7)``: torch's CUDA kernel for a tensor divided by
+                 a Python scalar, and the reference's own HIP quantizer
+                 (int4_gemm_scaled.hip:210-211).
+    ``t / scale`` is a true division in both (a tensor divisor), and
+    ``torch.round`` is round-half-even (numpy ``rint``).
+    """
+    t = np.asarray(t, dtype=np.float32)
+    K = t.shape[-1]
+    assert K % block == 0, f"last dim {K} not divisible by block {block}"
+    tb = t.reshape(-1, K // block, block)
+    amax = np.maximum(np.abs(tb).max(axis=-1, keepdims=True), np.float32(1e-8))
+    if div_mode == "true":
+        scale = (amax / np.float32(7.0)).astype(np.float32)
+    elif div_mode == "recip":
+        scale = (amax * (np.float32(1.0) / np.float32(7.0))).astype(np.float32)
+    else:
+        raise ValueError(f"div_mode must be 'true' or 'recip', got {div_mode!r}")
+    codes = np.clip(np.rint(tb / scale), -8, 7).astype(np.int32).reshape(-1, K)
+    packed = pack_int4_codes(codes)
+    rows = t.shape[:-1]
+    return (np.ascontiguousarray(packed.reshape(*rows, K // 2)),
+            np.ascontiguousarray(scale.reshape(*rows, K // block)))
+
+
+def repack_q4_0_native(raw: np.ndarray, out_features: int, in_features: int, block: int = BLOCK):
+    """Reference ``ops.repack_q4_0_native`` (ops.py:129-164): a lossless bit
+    shuffle of ggml Q4_0 blocks into the native layout. native nibble =
+    (u - 8) & 0xF, fp32 scale = float(fp16 d)."""
+    nb = in_features // block
+    total = out_features * nb
+    blocks = np.ascontiguousarray(raw).view(np.uint8).reshape(total, Q4_0_BLOCK_BYTES)
+    scale = blocks[:, :2].copy().view(np.float16).reshape(total).astype(np.float32)
+    qs = blocks[:, 2:].astype(np.int32)
+    lo = ((qs & 0xF) - 8) & 0xF
+    hi = (((qs >> 4) & 0xF) - 8) & 0xF
+    elems = np.empty((total, block), dtype=np.int32)
+    elems[:, : block // 2] = lo
+    elems[:, block // 2:] = hi
+    packed = (elems[:, 0::2] | (elems[:, 1::2] << 4)).astype(np.uint8).view(np.int8)
+    return (np.ascontiguousarray(packed.reshape(out_features, in_features // 2)),
+            np.ascontiguousarray(scale.reshape(out_features, nb)))
+
+
+def build_q4_0_bytes(u: np.ndarray, d_f16: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """Serialise offset-8 codes u uint8 [N, K] (0..15) and fp16 scales
+    [N, K/32] into raw ggml Q4_0 bytes (the format ops.py:138-140 reads)."""
+    N, K = u.shape
+    nb = K // block
+    ub = np.asarray(u, dtype=np.uint8).reshape(N * nb, block)
+    out = np.empty((N * nb, Q4_0_BLOCK_BYTES), dtype=np.uint8)
+    out[:, :2] = np.asarray(d_f16, dtype=np.float16).reshape(N * nb, 1).view(np.uint8).reshape(N * nb, 2)
+    out[:, 2:] = (ub[:, : block // 2] & 0xF) | ((ub[:, block // 2:] & 0xF) << 4)
+    return out.reshape(-1)
+
+
+def dequant_int4(packed: np.ndarray, scale: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """Reference dequant (int4_train_test.py:46-52, nodes.py:51): fp32
+    ``code * scale``, one IEEE multiply per element."""
+    codes = unpack_int4_codes(packed).astype(np.float32)
+    s = np.asarray(scale, dtype=np.float32)
+    return (codes.reshape(s.shape + (block,)) * s[..., None]).reshape(codes.shape)
+
+
+def dequant_int4_bf16_bits(packed: np.ndarray, scale: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """The bf16 weight the W4A16 emulation feeds its matmul: the fp32 product
+    rounded to bf16 (nodes.py:51-52 ``(q * scale).to(bfloat16)``)."""
+    return f32_to_bf16_bits(dequant_int4(packed, scale, block))
+
+
+def quantize_dequantize_int4(t: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """Reference ``nodes.quantize_dequantize_int4`` (nodes.py:43-52), fp32
+    result before its final ``.to(t.dtype)``."""
+    t = np.asarray(t, dtype=np.float32)
+    K = t.shape[-1]
+    if K % block != 0:
+        return t
+    tb = t.reshape(-1, K // block, block)
+    amax = np.maximum(np.abs(tb).max(axis=-1, keepdims=True), np.float32(1e-8))
+    scale = (amax / np.float32(7.0)).astype(np.float32)
+    # q stays a float here (no packing), so a negative input that rounds to
+    # zero keeps its sign: -0.0 * scale = -0.0, exactly as nodes.py:50-52.
+    q = np.clip(np.rint(tb / scale), np.float32(-8), np.float32(7)).astype(np.float32)
+    return (q * scale).reshape(t.shape)
+
+
+# ---------------------------------------------------------------------------
+# int8 (reference csrc/int8_gemm.hip:217-246, develop/harness/bench_int8.py:32-43)
+# ---------------------------------------------------------------------------
+def quantize_int8(x: np.ndarray, block: int = BLOCK):
+    """Restatement of ``quantize_int8_kernel`` (int8_gemm.hip:217-246): per
+    32-block s = max(amax, 1e-8) * (1/127) (reciprocal multiply, as the
+    kernel writes it), q = clamp(rint(v / s), -127, 127). Parity unpinned
+    against the HIP kernel itself (it cannot run here)."""
+    x = np.asarray(x, dtype=np.float32)
+    K = x.shape[-1]
+    xb = x.reshape(-1, K // block, block)
+    amax = np.maximum(np.abs(xb).max(axis=-1, keepdims=True), np.float32(1e-8))
+    s = (amax * (np.float32(1.0) / np.float32(127.0))).astype(np.float32)
+    q = np.clip(np.rint(xb / s), -127, 127).astype(np.int8).reshape(x.shape)
+    return q, np.ascontiguousarray(s.reshape(x.shape[:-1] + (K // block,)))
+
+
+def dequant_int8(q: np.ndarray, s: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """bench_int8.py:32-33: ``q.float().reshape(rows, -1, 32) * s[..., None]``."""
+    qf = np.asarray(q).astype(np.float32)
+    return (qf.reshape(qf.shape[0], -1, block) * np.asarray(s, np.float32)[..., None]).reshape(qf.shape)
+
+
+# ---------------------------------------------------------------------------
+# GEMM oracles (fp32 dequant then fp32 matmul: bench_int8.py:43)
+# ---------------------------------------------------------------------------
+def w4a16_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None) -> np.ndarray:
+    """``Y = X.float() @ dequant(W).T (+ bias)`` in fp32."""
+    w = dequant_int4(packed, scale)
+    y = np.asarray(x, dtype=np.float32) @ w.T
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float32)
+    return y
+
+
+def w8a16_matmul(x: np.ndarray, q: np.ndarray, s: np.ndarray, bias=None) -> np.ndarray:
+    w = dequant_int8(q, s)
+    y = np.asarray(x, dtype=np.float32) @ w.T
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float32)
+    return y
+
+
+def torch_cpu_dequant(packed, scale, block: int = BLOCK):
+    """The reference's dequant as torch CPU ops (int4_train_test.py:46-52):
+    words >> shifts & 0xF, sign fix, ``codes * scale.repeat_interleave``.
+    Used as the timed CPU path (multi-threaded like the reference's)."""
+    import torch
+    words = packed.contiguous().view(torch.int32)
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32)
+    nib = (words[..., None] >> shifts) & 0xF
+    codes = torch.where(nib > 7, nib - 16, nib).reshape(packed.shape[0], -1).float()
+    return codes * scale.repeat_interleave(block, dim=1)
+
+
+def torch_cpu_w4a16(x, packed, scale, bias=None):
+    """The reference's CPU torch path: dequant then fp32 ``torch.matmul``
+    (bench_int8.py:43 pattern)."""
+    import torch
+    y = torch.matmul(x.float(), torch_cpu_dequant(packed, scale).t())
+    return y + bias.float() if bias is not None else y
+
+
+def parity_metrics(got: np.ndarray, ref: np.ndarray) -> dict:
+    """The north-star parity measures: max|d| / max|ref| and the mean
+    relative error defined as mean|d| / mean|ref|."""
+    g = np.asarray(got, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    d = np.abs(g - r)
+    max_ref = float(np.abs(r).max()) if r.size else 0.0
+    mean_ref = float(np.abs(r).mean()) if r.size else 0.0
+    return {
+        "max_abs_over_max_ref": float(d.max()) / max_ref if max_ref > 0 else float(d.max() if d.size else 0.0),
+        "mean_rel": float(d.mean()) / mean_ref if mean_ref > 0 else float(d.mean() if d.size else 0.0),
+        "nonfinite": int((~np.isfinite(g)).sum()),
+    }

@@ -1,0 +1,159 @@
+"""W4A16 GEMM parity on the GPU, called through the C ABI (ops.gemm_w4a16 ->
+ctypes -> w4a16_gemm), against the oracle's fp32 dequant-then-matmul.
+
+Tolerances are the north-star bar, with the mean relative error defined as
+mean|got - ref| / mean|ref|:  max|d| <= 2e-2 * max|ref|  and  mean_rel <= 5e-3.
+fp32-output cases also check a much tighter bound where the kernel's math is
+exact up to fp32 rounding (the split-K kernel scales exact integer-code MMA
+partials in fp32)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from comfy_ui_gfx906_tools_b200 import ops, synthetic
+
+pytestmark = pytest.mark.gpu
+
+MAX_TOL = 2e-2
+MEAN_TOL = 5e-3
+
+
+def _weights(N, K, seed, dev):
+    raw, _, _ = synthetic.q4_0_weight(N, K, seed)
+    p, s = O.repack_q4_0_native(raw.numpy(), N, K)
+    return p, s, torch.from_numpy(p).to(dev), torch.from_numpy(s).to(dev)
+
+
+def _x(M, K, seed, dev):
+    x = synthetic.activations(M, K, seed)
+    return x.float().numpy(), x.to(dev)
+
+
+def _check(got, ref, max_tol=MAX_TOL, mean_tol=MEAN_TOL):
+    m = O.parity_metrics(got, ref)
+    assert m["nonfinite"] == 0, m
+    assert m["max_abs_over_max_ref"] <= max_tol, m
+    assert m["mean_rel"] <= mean_tol, m
+    return m
+
+
+def test_gemm_golden_vector(cuda, golden):
+    x = torch.from_numpy(golden["gemm_x_bits"].view(np.int16)).view(torch.bfloat16).to(cuda)
+    b = torch.from_numpy(golden["gemm_bias_bits"].view(np.int16)).view(torch.bfloat16).to(cuda)
+    p = torch.from_numpy(golden["q40_packed"]).to(cuda)
+    s = torch.from_numpy(golden["q40_scale"]).to(cuda)
+    y = ops.gemm_w4a16(x, p, s, b.float(), torch.float32)
+    _check(y.cpu().numpy(), golden["gemm_y_f32"], 1e-5, 1e-5)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 40, 64])
+@pytest.mark.parametrize("N,K", [(384, 512), (200, 96), (1000, 3072)])
+def test_gemm_small_m(cuda, M, N, K):
+    p, s, pd, sd = _weights(N, K, seed=N + K, dev=cuda)
+    xn, xd = _x(M, K, seed=M, dev=cuda)
+    ref = O.w4a16_matmul(xn, p, s)
+    y32 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32)
+    _check(y32.cpu().numpy(), ref, 1e-5, 1e-5)
+    ybf = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    _check(ybf.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 12])
+def test_gemm_splits_agree(cuda, splits):
+    N, K, M = 640, 3072, 16
+    p, s, pd, sd = _weights(N, K, 1, cuda)
+    xn, xd = _x(M, K, 2, cuda)
+    ref = O.w4a16_matmul(xn, p, s)
+    y = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=splits)
+    _check(y.cpu().numpy(), ref, 1e-5, 1e-5)
+
+
+def test_gemm_deterministic_and_workspace_rearmed(cuda):
+    N, K, M = 512, 6144, 5
+    p, s, pd, sd = _weights(N, K, 3, cuda)
+    _, xd = _x(M, K, 4, cuda)
+    y1 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=6)
+    y2 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=6)
+    y3 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=6)
+    assert torch.equal(y1, y2) and torch.equal(y2, y3)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_gemm_bias_and_out_dtypes(cuda, out_dtype):
+    N, K, M = 264, 1024, 9
+    p, s, pd, sd = _weights(N, K, 5, cuda)
+    xn, xd = _x(M, K, 6, cuda)
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(1)) * 0.1).to(out_dtype)
+    ref = O.w4a16_matmul(xn, p, s, bias.float().numpy())
+    for splits in (0, 1, 4):
+        y = ops.gemm_w4a16(xd, pd, sd, bias.to(cuda), out_dtype, splits=splits)
+        assert y.dtype == out_dtype
+        _check(y.float().cpu().numpy(), ref)
+
+
+def test_gemm_f16_scales_identical(cuda):
+    # Q4_0-sourced fp32 scales are exact fp16 values: the fp16 scale path gives bit-identical output
+    N, K, M = 768, 3072, 16
+    p, s, pd, sd = _weights(N, K, 8, cuda)
+    _, xd = _x(M, K, 9, cuda)
+    s16 = ops.scales_to_f16_if_exact(sd)
+    assert s16 is not None
+    for splits in (0, 1):
+        a = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=splits)
+        b = ops.gemm_w4a16(xd, pd, s16, None, torch.float32, splits=splits)
+        assert torch.equal(a, b)
+
+
+def test_gemm_general_rtn_weights(cuda):
+    # quantize_pack_int4 (RTN) weights carry general fp32 scales
+    N, K, M = 333, 640, 12
+    w = synthetic.float_weight(N, K, 12)
+    p, s = O.quantize_pack_int4(w.numpy())
+    xn, xd = _x(M, K, 13, cuda)
+    ref = O.w4a16_matmul(xn, p, s)
+    y = ops.gemm_w4a16(xd, torch.from_numpy(p).to(cuda), torch.from_numpy(s).to(cuda), None, torch.float32)
+    _check(y.cpu().numpy(), ref, 1e-5, 1e-5)
+
+
+def test_gemm_m_zero(cuda):
+    p, s, pd, sd = _weights(64, 64, 1, cuda)
+    y = ops.gemm_w4a16(torch.empty(0, 64, dtype=torch.bfloat16, device=cuda), pd, sd, None, torch.bfloat16)
+    assert y.shape == (0, 64)
+
+
+def test_gemm_rejects_bad_inputs(cuda):
+    p, s, pd, sd = _weights(64, 64, 1, cuda)
+    x = torch.zeros(2, 64, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(RuntimeError, match="inputs must be on device"):
+        ops.gemm_w4a16(x.cpu(), pd, sd, None, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="bias dtype"):
+        ops.gemm_w4a16(x, pd, sd, torch.zeros(64, device=cuda), torch.bfloat16)
+    with pytest.raises(RuntimeError, match=r"scales must be \[N, K/32\]"):
+        ops.gemm_w4a16(x, pd, sd[:, :1], None, torch.bfloat16)
+
+
+@pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
+@pytest.mark.parametrize("M", [1, 16])
+def test_gemm_flux_shapes_small_m_full_size(cuda, name, K, N, M):
+    p, s, pd, sd = _weights(N, K, seed=K * 7 + N, dev=cuda)
+    xn, xd = _x(M, K, seed=M + 100, dev=cuda)
+    ref = O.w4a16_matmul(xn, p, s)
+    y = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    _check(y.float().cpu().numpy(), ref)
+
+
+def test_int4_linear_module(cuda):
+    # Gfx906Int4Ops.Linear with Q4_0-sourced buffers, leading batch dims, bias in x.dtype
+    N, K = 256, 512
+    p, s, pd, sd = _weights(N, K, 21, cuda)
+    lin = ops.Gfx906Int4Ops.Linear(K, N, bias=True, device=cuda, dtype=torch.bfloat16)
+    lin.weight_q4.copy_(pd)
+    lin.weight_scale.copy_(sd)
+    with torch.no_grad():
+        lin.bias.copy_(torch.linspace(-1, 1, N))
+    x = synthetic.activations(2 * 7, K, 22).reshape(2, 7, K)
+    y = lin(x.to(cuda))
+    assert y.shape == (2, 7, N) and y.dtype == torch.bfloat16
+    ref = O.w4a16_matmul(x.float().reshape(-1, K).numpy(), p, s, lin.bias.float().cpu().numpy())
+    _check(y.float().reshape(-1, N).cpu().numpy(), ref)
