@@ -9,6 +9,9 @@
 namespace gfx {
 
 constexpr int kMaxSplits = 16;
+// Split-K arrival counters occupy this many bytes at the start of the
+// workspace (65536 tiles); the fp32 partials follow.
+constexpr size_t kSplitKCounterBytes = 256 * 1024;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

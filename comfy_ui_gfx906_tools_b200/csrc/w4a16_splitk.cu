@@ -343,8 +343,7 @@ size_t splitk_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
   SplitKPlan p = splitk_plan(M, N, K, splits_req, sms);
   if (p.splits <= 1) return 0;
   const size_t part = (size_t)p.splits * p.tok_blocks * p.tok * N * sizeof(float);
-  const size_t cnt = (size_t)p.tok_blocks * p.row_blocks * sizeof(int);
-  return align_up(part, 256) + align_up(cnt, 256);
+  return kSplitKCounterBytes + align_up(part, 256);
 }
 
 int splitk_auto_splits(int M, int N, int K, int sms) { return splitk_plan(M, N, K, 0, sms).splits; }
@@ -398,9 +397,14 @@ int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(GFX_ERR_WORKSPACE, "w4a16_gemm: split-K workspace of %zu bytes required, got %zu (ptr %p)",
                        need, workspace_bytes, workspace);
-    const size_t part_bytes = align_up((size_t)p.splits * p.tok_blocks * p.tok * N * sizeof(float), 256);
-    part = reinterpret_cast<float*>(workspace);
-    cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + part_bytes);
+    if ((size_t)p.tok_blocks * p.row_blocks * sizeof(int) > kSplitKCounterBytes)
+      return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm: %d x %d split-K tiles exceed the %zu-byte counter region",
+                       p.tok_blocks, p.row_blocks, kSplitKCounterBytes);
+    // Counters live at a fixed offset (the first kSplitKCounterBytes) so that
+    // calls of any shape sharing one workspace always find them re-armed to
+    // zero; the fp32 partials follow and need no initial value.
+    cnt = reinterpret_cast<int*>(workspace);
+    part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kSplitKCounterBytes);
   }
   CUtensorMap map;
   int rc = make_tmap_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,

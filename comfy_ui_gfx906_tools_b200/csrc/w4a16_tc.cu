@@ -1,6 +1,37 @@
 // W4A16 large-M GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
-// Placeholder until the tcgen05 kernel lands: reports "unsupported" so the
-// dispatcher keeps every shape on the split-K kernel.
+//
+// y[M, N] = x[M, K] @ bf16(code[N, K] * scale[N, K/32])^T (+ bias)
+//
+// Reference counterpart: int4_gemm_kernel (nodes/ComfyUI-Gfx906Int4/csrc/
+// int4_gemm_scaled.hip:53-180) behind gemm_int4 (binding.cpp:73-112) for the
+// large-M DiT linears. Same weight buffers; the weights are dequantized to the
+// bf16 values the reference's W4A16 emulation multiplies with (nodes.py:43-52),
+// bit for bit, and multiplied on the tensor cores with fp32 accumulation.
+//
+// Design (one persistent CTA per SM, 14 warps, swap-AB):
+//   D[n, m] (TMEM, 128 lanes = weight rows, 256 fp32 columns = tokens)
+//     = W_tile[128 x K] (A, dequantized bf16 in SMEM, K-major SWIZZLE_128B)
+//     * X_tile[256 x K]^T (B, bf16 in SMEM via TMA, K-major SWIZZLE_128B)
+//   Putting the 128-row weight tile on the MMA's M side lets one dequantized
+//   weight element feed 256 tokens, which halves the dequant work per FLOP
+//   compared with a 128-token tile.
+//   warp 4      TMA producer: x tile (TMA, 32 KB), nibble tile (TMA, 4 KB,
+//               SWIZZLE_32B) and group scales (cp.async) per 64-wide K stage.
+//   warps 6-13  dequant: each thread turns 32 nibbles of one weight row into
+//               bf16 in the UMMA canonical SW128 layout, then a proxy fence
+//               and an mbarrier arrival hand the stage to the MMA.
+//   warp 5      TMEM allocation + one elected thread issuing tcgen05.mma
+//               (M=128, N=256, K=16; 4 per stage) and tcgen05.commit.
+//   warps 0-3   epilogue: tcgen05.ld of the accumulator (warp w owns TMEM
+//               lanes 32w..32w+31), + bias, convert, store. The accumulator
+//               is double-buffered (2 x 256 columns = all 512), so the
+//               epilogue of tile i overlaps the main loop of tile i+1.
+// Exact dequant: with fp16-valued scales the product code*scale is exact in
+// fp32 and one rounding to bf16 equals the reference's two roundings; it is
+// computed as fma.rn.bf16x2(code, s_hi, code * s_lo) with s = s_hi + s_lo
+// split into two bf16 parts (code * s_lo is exact in bf16), 2.5 ops per
+// element. General fp32 scales use an fp32 multiply then one cvt.rn to bf16.
+// Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -8,14 +39,392 @@ namespace gfx {
 
 GFX_DEFINE_STATUS_READER(tc_device_status)
 
-bool w4a16_tc_supported(int M, int N, int K, int scale_dtype) {
-  (void)M; (void)N; (void)K; (void)scale_dtype;
-  return false;
+namespace tc {
+
+constexpr int kTileN = 128;       // weight rows per tile (MMA M)
+constexpr int kTileM = 256;       // tokens per tile (MMA N)
+constexpr int kStageK = 64;       // K per pipeline stage (one 128-byte swizzle row of bf16)
+constexpr int kUmmaK = 16;
+constexpr int kStages = 4;
+constexpr int kThreads = 14 * 32;
+constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6, kDequantWarps = 8;
+constexpr int kAccCols = kTileM;  // fp32 columns per accumulator
+constexpr int kTmemCols = 2 * kAccCols;
+
+constexpr int kXBytes = kTileM * kStageK * 2;       // 32 KB
+constexpr int kWBytes = kTileN * kStageK * 2;       // 16 KB
+constexpr int kNibBytes = kTileN * kStageK / 2;     // 4 KB
+constexpr int kScaleBytes = 1024;                   // 128 rows x 2 groups x 4 B
+constexpr int kStageBytes = kXBytes + kWBytes + kNibBytes + kScaleBytes;
+constexpr int kBarrierBytes = 256;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileM >> 3) << 17) |
+                            ((uint32_t)(kTileN >> 4) << 24);
+
+// SMEM matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-int launch_w4a16_tc(const void*, const void*, const void*, int, const void*, void*, int, int, int, int, cudaStream_t,
-                    int) {
-  return set_error(GFX_ERR_UNSUPPORTED, "w4a16 tcgen05 kernel not built");
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// One 32-bit nibble word (elements 8j..8j+7 of a row) -> 8 bf16 = 16 bytes.
+template <bool kF16Scale>
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, float s, uint32_t s_hi2, uint32_t s_lo2) {
+  uint32_t out[4];
+  if constexpr (kF16Scale) {
+    const uint32_t t2 = w >> 4;
+    constexpr uint32_t kOne = 0x3F803F80u, kMinus136 = 0xC308C308u;  // bf16x2 (1, 1), (-136, -136)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      // nibbles 2p (bits 0-3) and 2p+1 (bits 16-19), offset-8 magic 0x4300|u = 128+u
+      const uint32_t t = prmt(w, t2, 0x0400u + 0x0101u * p);
+      const uint32_t magic = and_xor(t, 0x000F000Fu, 0x43084308u);
+      const uint32_t code = bf16x2_fma(magic, kOne, kMinus136);   // exact integer codes
+      const uint32_t lo = bf16x2_mul(code, s_lo2);                  // exact (<= 7 significant bits)
+      out[p] = bf16x2_fma(code, s_hi2, lo);                         // RN(code * s), one rounding
+    }
+  } else {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t n0 = (w >> (8 * p)) & 0xFu, n1 = (w >> (8 * p + 4)) & 0xFu;
+      const float c0 = __uint_as_float(0x4B000000u | (n0 ^ 8u)) - 8388616.0f;  // exact code
+      const float c1 = __uint_as_float(0x4B000000u | (n1 ^ 8u)) - 8388616.0f;
+      out[p] = pack_bf16x2_rn(__fmul_rn(c0, s), __fmul_rn(c1, s));
+    }
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+struct Smem {
+  uint8_t* stage0;     // stage s starts at stage0 + s * kStageBytes
+  uint64_t* full;      // [kStages] TMA + cp.async landed
+  uint64_t* wready;    // [kStages] dequantized weights written
+  uint64_t* empty;     // [kStages] MMAs done reading the stage
+  uint64_t* acc_full;  // [2]
+  uint64_t* acc_empty; // [2]
+  uint64_t* drain;     // [1]
+  uint32_t* tmem_base;
+};
+
+template <bool kF16Scale, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_constant__ CUtensorMap x_map,
+                                                               const __grid_constant__ CUtensorMap nib_map,
+                                                               const void* __restrict__ wscale,
+                                                               const OutT* __restrict__ bias, OutT* __restrict__ y,
+                                                               int M, int N, int K) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem sm;
+  sm.stage0 = base;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+  sm.full = bars;
+  sm.wready = bars + kStages;
+  sm.empty = bars + 2 * kStages;
+  sm.acc_full = bars + 3 * kStages;
+  sm.acc_empty = bars + 3 * kStages + 2;
+  sm.drain = bars + 3 * kStages + 4;
+  sm.tmem_base = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_n = (N + kTileN - 1) / kTileN;
+  const int tiles_m = (M + kTileM - 1) / kTileM;
+  const int num_tiles = tiles_n * tiles_m;
+  const int k_stages = (K + kStageK - 1) / kStageK;
+  const int groups = K >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1 + 32);
+      mbar_init(&sm.wready[s], kDequantWarps);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], kEpiWarps);
+    }
+    mbar_init(sm.drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) tmem_alloc(sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sm.tmem_base;
+
+  bool ok = true;
+  if (warp == kProducerWarp) {
+    // -------------------------------- producer --------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&x_map);
+      tma_prefetch_desc(&nib_map);
+    }
+    uint32_t kit = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int n0 = (tile % tiles_n) * kTileN;
+      const int m0 = (tile / tiles_n) * kTileM;
+      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        const int s = kit % kStages;
+        const uint32_t ph = (kit / kStages) & 1;
+        if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+        uint8_t* st = sm.stage0 + s * kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.full[s], kXBytes + kNibBytes);
+          tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
+          tma_load_2d(st + kXBytes + kWBytes, &nib_map, &sm.full[s], ks * (kStageK / 2), n0);
+        }
+        uint8_t* sc = st + kXBytes + kWBytes + kNibBytes;
+        const int g0 = ks * 2;
+        if (kF16Scale) {
+          // one 4-byte word = the two fp16 scales of a row; smem layout [row]
+#pragma unroll
+          for (int j = 0; j < kTileN / 32; ++j) {
+            const int r = lane + 32 * j, n = n0 + r;
+            const bool valid = n < N && g0 < groups;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+            if (valid) src += ((size_t)n * groups + g0) * 2;
+            cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
+          }
+        } else {
+          // smem layout [group][row] (conflict-free reads)
+#pragma unroll
+          for (int j = 0; j < 2 * kTileN / 32; ++j) {
+            const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
+            const bool valid = n < N && (g0 + g) < groups;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+            if (valid) src += ((size_t)n * groups + g0 + g) * 4;
+            cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
+          }
+        }
+        cp_async_mbar_arrive_noinc(&sm.full[s]);
+      }
+    }
+  } else if (warp >= kDequantWarp0) {
+    // -------------------------------- dequant ---------------------------------
+    const int dt = (warp - kDequantWarp0) * 32 + lane;  // 0..255
+    const int g = dt / kTileN;                          // group within the stage
+    const int r = dt % kTileN;                          // weight row within the tile
+    uint32_t kit = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        const int s = kit % kStages;
+        const uint32_t ph = (kit / kStages) & 1;
+        if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
+        uint8_t* st = sm.stage0 + s * kStageBytes;
+        const uint8_t* nib = st + kXBytes + kWBytes;
+        const uint8_t* sc = nib + kNibBytes;
+        // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
+        const uint4 q = *reinterpret_cast<const uint4*>(nib + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
+        float sf;
+        uint32_t s_hi2 = 0, s_lo2 = 0;
+        if (kF16Scale) {
+          sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
+          const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
+          const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
+          const uint32_t hb = __float_as_uint(hi) >> 16;
+          const uint32_t lb = __float_as_uint(lo) >> 16;  // exact truncation (low bits are zero)
+          s_hi2 = hb | (hb << 16);
+          s_lo2 = lb | (lb << 16);
+        } else {
+          sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
+        }
+        uint8_t* wrow = st + kXBytes + r * 128;
+        const int c0 = 4 * g, sw = r & 7;
+        *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = dequant_word<kF16Scale>(q.x, sf, s_hi2, s_lo2);
+        *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = dequant_word<kF16Scale>(q.y, sf, s_hi2, s_lo2);
+        *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = dequant_word<kF16Scale>(q.z, sf, s_hi2, s_lo2);
+        *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = dequant_word<kF16Scale>(q.w, sf, s_hi2, s_lo2);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.wready[s]);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------- MMA -----------------------------------
+    uint32_t kit = 0;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      if (!mbar_wait(&sm.acc_empty[acc], aph ^ 1, kDevErrMmaBarrierTimeout)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + acc * kAccCols;
+      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        const int s = kit % kStages;
+        const uint32_t ph = (kit / kStages) & 1;
+        if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout) ||
+            !mbar_wait(&sm.wready[s], ph, kDevErrFullBarrierTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t xa = smem_u32(sm.stage0 + s * kStageBytes);
+          const uint32_t wa = xa + kXBytes;
+          const uint64_t adesc = sw128_desc(wa), bdesc = sw128_desc(xa);
+#pragma unroll
+          for (int k = 0; k < kStageK / kUmmaK; ++k) {
+            // advance 16 elements (32 bytes) along K inside the swizzle atom
+            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc, (ks | k) != 0);
+          }
+          umma_commit(&sm.empty[s]);
+          if (ks == k_stages - 1) umma_commit(&sm.acc_full[acc]);
+        }
+        __syncwarp();
+      }
+    }
+    // drain: every MMA this thread issued has completed before TMEM is freed
+    if (lane == 0) umma_commit(sm.drain);
+    __syncwarp();
+    mbar_wait(sm.drain, 0, kDevErrMmaBarrierTimeout);
+  } else {
+    // -------------------------------- epilogue --------------------------------
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+      const int n0 = (tile % tiles_n) * kTileN;
+      const int m0 = (tile / tiles_n) * kTileM;
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      if (!mbar_wait(&sm.acc_full[acc], aph, kDevErrEpilogueBarrierTimeout)) { ok = false; break; }
+      tc_fence_after();
+      const int n = n0 + warp * 32 + lane;
+      const bool n_ok = n < N;
+      const float b = (bias != nullptr && n_ok) ? to_f32(bias[n]) : 0.0f;
+      const uint32_t taddr = tmem + acc * kAccCols + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kAccCols; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c, v);
+        const int mbase = m0 + c;
+        if (n_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = mbase + j;
+            if (m < M) y[(size_t)m * N + n] = from_f32<OutT>(__uint_as_float(v[j]) + b);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+bool w4a16_tc_supported(int M, int N, int K, int scale_dtype) {
+  (void)N;
+  if (M <= 64) return false;  // the split-K kernel owns the HBM-bound small-M regime
+  if (K % 32 != 0) return false;
+  if (scale_dtype == GFX_SCALE_F16 && K % 64 != 0) return false;
+  return true;
+}
+
+template <bool F16S, typename OutT>
+static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& nm, const void* ws, const void* bias, void* y, int M,
+                       int N, int K, cudaStream_t st, int sms) {
+  auto kern = tc::w4a16_tc_kernel<F16S, OutT>;
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
+    if (e != cudaSuccess)
+      return set_error(GFX_ERR_CUDA, "w4a16_tc: cannot set %d bytes of shared memory: %s", tc::kSmemBytes,
+                       cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const int tiles = ((N + tc::kTileN - 1) / tc::kTileN) * ((M + tc::kTileM - 1) / tc::kTileM);
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, tc::kThreads, tc::kSmemBytes, st>>>(xm, nm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
+  return check_launch("w4a16_tc_kernel");
+}
+
+int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
+  CUtensorMap xm, nm;
+  int rc = make_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+                        tc::kStageK, tc::kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&nm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                    tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  const bool f16 = scale_dtype == GFX_SCALE_F16;
+  if (out_dtype == GFX_DTYPE_F32)
+    return f16 ? launch_tc_t<true, float>(xm, nm, ws, bias, y, M, N, K, stream, sms)
+               : launch_tc_t<false, float>(xm, nm, ws, bias, y, M, N, K, stream, sms);
+  if (out_dtype == GFX_DTYPE_F16)
+    return f16 ? launch_tc_t<true, __half>(xm, nm, ws, bias, y, M, N, K, stream, sms)
+               : launch_tc_t<false, __half>(xm, nm, ws, bias, y, M, N, K, stream, sms);
+  return f16 ? launch_tc_t<true, __nv_bfloat16>(xm, nm, ws, bias, y, M, N, K, stream, sms)
+             : launch_tc_t<false, __nv_bfloat16>(xm, nm, ws, bias, y, M, N, K, stream, sms);
 }
 
 }  // namespace gfx

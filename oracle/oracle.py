@@ -36,6 +36,7 @@ __all__ = [
     "quantize_pack_int4", "repack_q4_0_native", "dequant_int4", "dequant_int4_bf16_bits",
     "quantize_dequantize_int4", "build_q4_0_bytes", "w4a16_matmul", "quantize_int8",
     "dequant_int8", "w8a16_matmul", "parity_metrics", "unpack_int4_codes", "pack_int4_codes",
+    "torch_cpu_dequant", "torch_cpu_w4a16", "w4a16_matmul_bf16w",
 ]
 
 
@@ -210,6 +211,18 @@ def dequant_int8(q: np.ndarray, s: np.ndarray, block: int = BLOCK) -> np.ndarray
 def w4a16_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None) -> np.ndarray:
     """``Y = X.float() @ dequant(W).T (+ bias)`` in fp32."""
     w = dequant_int4(packed, scale)
+    y = np.asarray(x, dtype=np.float32) @ w.T
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float32)
+    return y
+
+
+def w4a16_matmul_bf16w(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None) -> np.ndarray:
+    """``Y = X.float() @ bf16(dequant(W)).T`` in fp32: the W4A16 emulation with
+    the weight rounded to bf16 (nodes.py:51-52 for a bf16 model). The
+    tensor-core kernel multiplies exactly these operands, so it matches this
+    oracle up to fp32 accumulation order."""
+    w = round_to_bf16(dequant_int4(packed, scale))
     y = np.asarray(x, dtype=np.float32) @ w.T
     if bias is not None:
         y = y + np.asarray(bias, dtype=np.float32)

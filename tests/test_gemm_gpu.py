@@ -155,5 +155,88 @@ def test_int4_linear_module(cuda):
     x = synthetic.activations(2 * 7, K, 22).reshape(2, 7, K)
     y = lin(x.to(cuda))
     assert y.shape == (2, 7, N) and y.dtype == torch.bfloat16
-    ref = O.w4a16_matmul(x.float().reshape(-1, K).numpy(), p, s, lin.bias.float().cpu().numpy())
+    ref = O.w4a16_matmul(x.float().reshape(-1, K).numpy(), p, s, lin.bias.detach().float().cpu().numpy())
     _check(y.float().reshape(-1, N).cpu().numpy(), ref)
+
+
+# ---------------------------------------------------------------------------
+# large M: the tcgen05 kernel (automatic path for M > 64)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("M", [65, 256, 300, 777])
+@pytest.mark.parametrize("N,K", [(384, 512), (200, 96), (1000, 3072), (129, 64)])
+@pytest.mark.parametrize("f16_scales", [False, True])
+def test_gemm_large_m_tcgen05(cuda, M, N, K, f16_scales):
+    if f16_scales and K % 64:
+        pytest.skip("fp16 scales need K % 64 == 0")
+    p, s, pd, sd = _weights(N, K, seed=N + K + 1, dev=cuda)
+    if f16_scales:
+        sd = ops.scales_to_f16_if_exact(sd)
+    xn, xd = _x(M, K, seed=M + 7, dev=cuda)
+    y32 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32).cpu().numpy()
+    # the kernel multiplies exactly bf16(code*scale): tight against that oracle
+    _check(y32, O.w4a16_matmul_bf16w(xn, p, s), 1e-5, 1e-5)
+    # and within the north-star bar against the fp32 dequant-then-matmul
+    _check(y32, O.w4a16_matmul(xn, p, s))
+    ybf = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    _check(ybf.float().cpu().numpy(), O.w4a16_matmul(xn, p, s))
+
+
+def test_gemm_large_m_general_fp32_scales(cuda):
+    N, K, M = 520, 1024, 400
+    w = synthetic.float_weight(N, K, 31)
+    p, s = O.quantize_pack_int4(w.numpy())
+    xn, xd = _x(M, K, 32, cuda)
+    y = ops.gemm_w4a16(xd, torch.from_numpy(p).to(cuda), torch.from_numpy(s).to(cuda), None, torch.float32)
+    _check(y.cpu().numpy(), O.w4a16_matmul_bf16w(xn, p, s), 1e-5, 1e-5)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_gemm_large_m_bias(cuda, out_dtype):
+    N, K, M = 300, 768, 333
+    p, s, pd, sd = _weights(N, K, 41, cuda)
+    xn, xd = _x(M, K, 42, cuda)
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(3)) * 0.1).to(out_dtype)
+    y = ops.gemm_w4a16(xd, pd, sd, bias.to(cuda), out_dtype)
+    assert y.dtype == out_dtype
+    _check(y.float().cpu().numpy(), O.w4a16_matmul(xn, p, s, bias.float().numpy()))
+
+
+def test_gemm_large_m_matches_splitk_path(cuda):
+    # splits=1 forces the split-K kernel; both paths agree within the bf16 weight rounding
+    N, K, M = 640, 2048, 512
+    p, s, pd, sd = _weights(N, K, 51, cuda)
+    _, xd = _x(M, K, 52, cuda)
+    a = ops.gemm_w4a16(xd, pd, sd, None, torch.float32).cpu().numpy()
+    b = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=1).cpu().numpy()
+    _check(a, b)
+
+
+def test_gemm_large_m_deterministic(cuda):
+    N, K, M = 768, 3072, 1024
+    p, s, pd, sd = _weights(N, K, 61, cuda)
+    _, xd = _x(M, K, 62, cuda)
+    y1 = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    y2 = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
+def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
+    """BASELINE config 2 at full size. The oracle checks 96 sampled token rows
+    exactly (all N outputs each) and every row through a size-independent
+    checksum: sum_n Y[m, n] == X[m] . sum_n W[n] (linearity), in fp64."""
+    M = 4608
+    p, s, pd, sd = _weights(N, K, seed=K * 3 + N, dev=cuda)
+    sd16 = ops.scales_to_f16_if_exact(sd)
+    x = synthetic.activations(M, K, seed=77)
+    y = ops.gemm_w4a16(x.to(cuda), pd, sd16, None, torch.bfloat16).float()
+    rows = np.random.default_rng(0).choice(M, 96, replace=False)
+    xs = x[rows].float().numpy()
+    got = y[torch.from_numpy(rows).to(cuda)].cpu().numpy()
+    _check(got, O.w4a16_matmul(xs, p, s))
+    _check(got, O.w4a16_matmul_bf16w(xs, p, s), 8e-3, 2.5e-3)  # bf16 output rounding only
+    wsum = O.round_to_bf16(O.dequant_int4(p, s)).astype(np.float64).sum(axis=0)   # [K]
+    want = x.float().numpy().astype(np.float64) @ wsum                             # [M]
+    gotsum = y.double().sum(dim=1).cpu().numpy()
+    scale = np.abs(x.float().numpy()).astype(np.float64) @ np.abs(wsum)
+    assert np.max(np.abs(gotsum - want) / (scale + 1e-30)) < 2e-3
