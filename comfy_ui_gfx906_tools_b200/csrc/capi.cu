@@ -136,9 +136,8 @@ int gfx_device_status(int clear) {
 
 size_t w4a16_workspace_bytes(int M, int N, int K, int splits) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const int sms = sm_count(current_device());
-  if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 0;
-  return splitk_workspace_bytes(M, N, K, splits, sms);
+  if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 0;  // the tensor-core path needs no scratch
+  return splitk_workspace_bytes(M, N, K, splits, sm_count(current_device()));
 }
 
 int w4a16_auto_splits(int M, int N, int K) {
@@ -155,7 +154,10 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
   if (M == 0) return GFX_OK;
   const int sms = sm_count(current_device());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (splits == 0 && w4a16_tc_supported(M, N, K, scale_dtype))
+  // M > 64 always runs on the tcgen05 kernel (its tiles cover K whole, so a
+  // requested split count only matters for the small-M kernel, as for the
+  // reference where `splits` changes speed, not the result's definition).
+  if (w4a16_tc_supported(M, N, K, scale_dtype))
     return launch_w4a16_tc(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, st, sms);
   return launch_w4a16_splitk(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, workspace,
                              workspace_bytes, st, sms);

@@ -1,0 +1,524 @@
+// W4A16 small-M GEMM (M <= 64): the HBM-bound weight stream, stream-K.
+//
+// y[M, N] = x[M, K] @ (code[N, K] * scale[N, K/32])^T (+ bias), x bf16.
+//
+// Reference counterpart: int4_gemm_kernel + splitk_reduce_kernel
+// (nodes/ComfyUI-Gfx906Int4/csrc/int4_gemm_scaled.hip:53-191) as called from
+// gemm_int4 (binding.cpp:73-112) with split-K for narrow problems
+// (auto_splits, binding.cpp:36-43). Same weight layout and scale format; the
+// design is B200-first:
+//
+//  * Work is a grid of units (128 weight rows x 256 K). CTA c of G takes the
+//    contiguous unit range [c*U/G, (c+1)*U/G) in row-block-major order
+//    ("stream-K"): every CTA streams the same number of weight bytes, so there
+//    is no partial last wave. An explicit split count S is the special case
+//    G = row_blocks * S (each row block cut into S equal K segments).
+//  * One producer warp streams each unit's nibbles (TMA, SWIZZLE_128B), group
+//    scales (TMA when the scale row stride is 16-byte aligned, else cp.async)
+//    and the matching 256-wide slice of the activations (TMA, SWIZZLE_128B
+//    boxes) into a shared-memory ring.
+//  * Eight consumer warps = 4 row slices (32 rows) x 2 K halves (4 of the 8
+//    32-groups of a unit). A warp reads one 32-bit nibble word per row with
+//    ldmatrix (conflict-free through the swizzle), turns nibbles into EXACT
+//    bf16 integer codes with one LOP3 + one bf16x2 FMA per pair (magic
+//    0x4300|u = 128+u), and runs mma.sync m16n8k16 with the weights as the
+//    16-row A operand and the tokens as the 8-column B operand. Each MMA pair
+//    covers exactly one 32-group, so its fp32 partial is scaled in registers
+//    (acc += partial * scale): the result is the fp32 dequant-then-matmul up
+//    to fp32 rounding (the weight operand is never rounded to bf16).
+//  * When a CTA leaves a row block (segment end) the two K halves are summed
+//    through shared memory. A row block covered by one CTA is stored directly
+//    (+bias). Otherwise each segment writes its fp32 partial to the workspace
+//    and bumps the row block's arrival counter; the last arrival (no spinning)
+//    sums the segments in segment order -- deterministic -- adds the bias,
+//    stores, and re-arms the counter to zero.
+//
+// K order inside one 16-wide MMA step is permuted (both operands alike) so
+// that each thread's weights come from one nibble word with no byte shuffles:
+// k-slot (2t, 2t+1) of step s holds elements (8t + 2s, 8t + 2s + 4) and slot
+// (2t + 8, 2t + 9) holds (8t + 2s + 1, 8t + 2s + 5) of the 32-group.
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gfx {
+
+namespace smallm {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kRows = 128;                      // weight rows per unit (4 slices x 32)
+constexpr int kStageK = 256;                    // K per unit
+constexpr int kStageBytesPerRow = kStageK / 2;  // 128 nibble bytes = one SW128 row
+constexpr int kGroupsPerStage = kStageK / 32;
+constexpr int kMT = 2;                          // m16 tiles per warp (32 rows)
+constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 consumer threads
+
+template <int NT, int STAGES, bool kF16Scale>
+struct Layout {
+  static constexpr int kTok = 8 * NT;
+  static constexpr int kNibBytes = kRows * kStageBytesPerRow;
+  static constexpr int kScaleRowBytes = kGroupsPerStage * (kF16Scale ? 2 : 4);  // dense [row][group]
+  static constexpr int kScaleBytes = (kRows * kScaleRowBytes + 1023) / 1024 * 1024;
+  static constexpr int kXBoxBytes = kTok * 128;  // one 64-wide k box (SW128)
+  static constexpr int kXBytes = (4 * kXBoxBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = kNibBytes + kScaleBytes + kXBytes;
+  static constexpr int kAcc = kMT * NT * 4;      // accumulators per thread
+  static constexpr int kRedBytes = 4 * 32 * kAcc * 4;  // K-half reduction, aliases a stage's nibbles
+  static_assert(kRedBytes <= kNibBytes, "reduction buffer must fit in a stage's nibble tile");
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + 2 * STAGES * 8 + 64;
+};
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1, const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %11, %12, %13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+// Two nibbles (at bit 0 and bit 16 of w_shifted) -> bf16x2 exact integer codes.
+__device__ __forceinline__ uint32_t nib_pair_to_bf16x2(uint32_t w_shifted) {
+  // (w & 0x000F000F) ^ 0x43084308 == 0x4300 | (nib ^ 8) per half: 128 + u, u = code + 8
+  const uint32_t magic = and_xor(w_shifted, 0x000F000Fu, 0x43084308u);
+  uint32_t c;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(c) : "r"(magic), "r"(0x3F803F80u), "r"(0xC308C308u));  // -136, exact
+  return c;
+}
+
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumerWarps * 32) : "memory");
+}
+
+// First CTA whose unit range contains unit t: largest c with floor(c*U/G) <= t.
+__device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
+  return (int)(((t + 1) * G + U - 1) / U) - 1;
+}
+
+template <int NT, int STAGES, bool kF16Scale, typename OutT>
+__global__ void __launch_bounds__(kThreads) w4a16_smallm_kernel(
+    const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
+    const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
+    const OutT* __restrict__ bias, OutT* __restrict__ y, float* __restrict__ partials, int* __restrict__ counters,
+    int M, int N, int K, int G, int max_segs) {
+  using L = Layout<NT, STAGES, kF16Scale>;
+  constexpr int kTok = L::kTok;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  int* s_flag = reinterpret_cast<int*>(empty + STAGES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tb = blockIdx.y;  // token block
+  const int tok0 = tb * kTok;
+  const int groups = K >> 5;
+  const int KS = (K + kStageK - 1) / kStageK;
+  const int RB = (N + kRows - 1) / kRows;
+  const long long U = (long long)RB * KS;
+  const int c = blockIdx.x;
+  const long long u_begin = (long long)c * U / G;
+  const long long u_end = (long long)(c + 1) * U / G;
+  const int n_iters = (int)(u_end - u_begin);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], scale_tma ? 1 : 1 + 32);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (n_iters <= 0) return;
+
+  bool ok = true;
+  if (warp == kConsumerWarps) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&nib_map);
+      tma_prefetch_desc(&x_map);
+      if (scale_tma) tma_prefetch_desc(&scale_map);
+    }
+    for (int it = 0; it < n_iters; ++it) {
+      const int stage = it % STAGES;
+      const uint32_t phase = (it / STAGES) & 1;
+      if (!mbar_wait(&empty[stage], phase ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+      const long long u = u_begin + it;
+      const int rb = (int)(u / KS), ks = (int)(u % KS);
+      uint8_t* st = smem + stage * L::kStageBytes;
+      uint8_t* sc = st + L::kNibBytes;
+      uint8_t* xs = sc + L::kScaleBytes;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[stage],
+                              L::kNibBytes + 4 * L::kXBoxBytes + (scale_tma ? kRows * L::kScaleRowBytes : 0));
+        tma_load_2d(st, &nib_map, &full[stage], ks * kStageBytesPerRow, rb * kRows);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          tma_load_2d(xs + b * L::kXBoxBytes, &x_map, &full[stage], ks * kStageK + b * 64, tok0);
+        if (scale_tma) tma_load_2d(sc, &scale_map, &full[stage], ks * kGroupsPerStage, rb * kRows);
+      }
+      if (!scale_tma) {
+        constexpr int kWordsPerRow = L::kScaleRowBytes / 4;
+        constexpr int kWords = kRows * kWordsPerRow;
+        for (int i = lane; i < kWords; i += 32) {
+          const int r = i / kWordsPerRow, wd = i % kWordsPerRow;
+          const int n = rb * kRows + r;
+          const int g = ks * kGroupsPerStage + wd * (kF16Scale ? 2 : 1);
+          const bool valid = (n < N) && (g < groups);
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+          if (valid) src += ((size_t)n * groups + g) * (kF16Scale ? 2 : 4);
+          cp_async_4(sc + 4 * i, src, valid ? 4u : 0u);
+        }
+        cp_async_mbar_arrive_noinc(&full[stage]);
+      }
+    }
+  } else {
+    // ------------------------------ consumers -----------------------------
+    const int rs = warp & 3;   // row slice: rows rs*32 .. rs*32+31 of the row block
+    const int kh = warp >> 2;  // K half: groups 4*kh .. 4*kh+3 of each unit
+    const int g_ = lane >> 2, t_ = lane & 3;
+    const int lm_i = lane >> 3, lm_j = lane & 7;
+    float acc[kMT][NT][4];
+#pragma unroll
+    for (int i = 0; i < kMT; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+
+    for (int it = 0; it < n_iters; ++it) {
+      const int stage = it % STAGES;
+      const uint32_t phase = (it / STAGES) & 1;
+      if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) { ok = false; break; }
+      const uint8_t* st = smem + stage * L::kStageBytes;
+      const uint32_t nib_base = smem_u32(st);
+      const uint8_t* sc = st + L::kNibBytes;
+      const uint8_t* xs = sc + L::kScaleBytes;
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp) {
+        const int gp = 4 * kh + 2 * pp;  // group pair (gp, gp+1), x box gp/2
+        uint32_t xf[2][NT][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int tok = nt * 8 + g_;
+            const int chunk = h * 4 + t_;
+            const uint4 v = *reinterpret_cast<const uint4*>(xs + (gp >> 1) * L::kXBoxBytes + tok * 128 +
+                                                            ((chunk ^ (tok & 7)) << 4));
+            xf[h][nt][0] = v.x; xf[h][nt][1] = v.y; xf[h][nt][2] = v.z; xf[h][nt][3] = v.w;
+          }
+        }
+        uint32_t w[kMT][4];
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) {
+          const int lrow = rs * 32 + mt * 16 + lm_j + (lm_i & 1) * 8;
+          const int lgrp = gp + (lm_i >> 1);
+          ldmatrix_x4(nib_base + lrow * kStageBytesPerRow + ((lgrp ^ (lrow & 7)) << 4), w[mt][0], w[mt][1],
+                      w[mt][2], w[mt][3]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t wr = w[mt][2 * h], wr8 = w[mt][2 * h + 1];
+            const int r_lo = rs * 32 + mt * 16 + g_, r_hi = r_lo + 8;
+            float s_r, s_r8;
+            if (kF16Scale) {
+              const __half* sch = reinterpret_cast<const __half*>(sc);
+              s_r = __half2float(sch[r_lo * kGroupsPerStage + gp + h]);
+              s_r8 = __half2float(sch[r_hi * kGroupsPerStage + gp + h]);
+            } else {
+              const float* scf = reinterpret_cast<const float*>(sc);
+              s_r = scf[r_lo * kGroupsPerStage + gp + h];
+              s_r8 = scf[r_hi * kGroupsPerStage + gp + h];
+            }
+            const uint32_t a00 = nib_pair_to_bf16x2(wr), a01 = nib_pair_to_bf16x2(wr8);
+            const uint32_t a02 = nib_pair_to_bf16x2(wr >> 4), a03 = nib_pair_to_bf16x2(wr8 >> 4);
+            const uint32_t a10 = nib_pair_to_bf16x2(wr >> 8), a11 = nib_pair_to_bf16x2(wr8 >> 8);
+            const uint32_t a12 = nib_pair_to_bf16x2(wr >> 12), a13 = nib_pair_to_bf16x2(wr8 >> 12);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint32_t* xv = xf[h][nt];
+              const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+              float p[4];
+              mma_bf16_16816(p, a00, a01, a02, a03, prmt(xv[0], xv[2], 0x5410), prmt(xv[0], xv[2], 0x7632), zero);
+              mma_bf16_16816(p, a10, a11, a12, a13, prmt(xv[1], xv[3], 0x5410), prmt(xv[1], xv[3], 0x7632), p);
+              acc[mt][nt][0] = fmaf(p[0], s_r, acc[mt][nt][0]);
+              acc[mt][nt][1] = fmaf(p[1], s_r, acc[mt][nt][1]);
+              acc[mt][nt][2] = fmaf(p[2], s_r8, acc[mt][nt][2]);
+              acc[mt][nt][3] = fmaf(p[3], s_r8, acc[mt][nt][3]);
+            }
+          }
+        }
+      }
+      // ---------------- segment end: leaving a row block (or the range) ----------------
+      const long long u = u_begin + it;
+      const bool seg_end = (((u + 1) % KS) == 0) || (it == n_iters - 1);
+      if (!seg_end) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        continue;
+      }
+      const int rb = (int)(u / KS);
+      const long long rb_lo = (long long)rb * KS, rb_hi = rb_lo + KS;
+      const long long seg_lo = u_begin > rb_lo ? u_begin : rb_lo;
+      const bool single = (seg_lo == rb_lo) && (u + 1 == rb_hi);
+      // The stage is still held (not yet released to the producer): its
+      // nibble tile doubles as the K-half reduction buffer once every
+      // consumer is done reading it.
+      float* red = reinterpret_cast<float*>(const_cast<uint8_t*>(st));
+      consumer_sync();
+      // 1) K halves -> kh 0 (through shared memory)
+      float* my_red = red + (rs * 32 + lane) * L::kAcc;
+      if (kh == 1) {
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) my_red[(mt * NT + nt) * 4 + e] = acc[mt][nt][e];
+      }
+      consumer_sync();
+      if (kh == 0) {
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][nt][e] += my_red[(mt * NT + nt) * 4 + e];
+      }
+      const int n0 = rb * kRows;
+      if (single) {
+        if (kh == 0) {
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int n = n0 + rs * 32 + mt * 16 + g_ + half * 8;
+              if (n >= N) continue;
+              const float b = bias ? to_f32(bias[n]) : 0.0f;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                  const int tok = tok0 + nt * 8 + 2 * t_ + cc;
+                  if (tok < M) y[(size_t)tok * N + n] = from_f32<OutT>(acc[mt][nt][half * 2 + cc] + b);
+                }
+            }
+        }
+      } else {
+        // 2) partial of this segment -> workspace slot [tb][rb][seg]
+        const int seg = c - owner_cta(rb_lo, U, G);
+        float* part = partials + (((size_t)tb * RB + rb) * max_segs) * (kTok * kRows);
+        if (kh == 0) {
+          float* mine = part + (size_t)seg * (kTok * kRows);
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int r = rs * 32 + mt * 16 + g_ + half * 8;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) mine[(nt * 8 + 2 * t_ + cc) * kRows + r] = acc[mt][nt][half * 2 + cc];
+            }
+          __threadfence();
+        }
+        consumer_sync();
+        int* counter = counters + (size_t)tb * RB + rb;
+        const int nsegs = owner_cta(rb_hi - 1, U, G) - owner_cta(rb_lo, U, G) + 1;
+        if (warp == 0 && lane == 0) *s_flag = (atomicAdd(counter, 1) == nsegs - 1);
+        consumer_sync();
+        if (*s_flag) {
+          __threadfence();
+          // 3) last arrival: fixed-order sum over the segments, + bias, store, re-arm
+          const int tc = threadIdx.x;  // 0..255 (consumers)
+          for (int i = tc; i < kTok * kRows; i += kConsumerWarps * 32) {
+            const int tok = i / kRows, r = i % kRows;
+            const int n = n0 + r;
+            if (n >= N || tok0 + tok >= M) continue;
+            float v = 0.0f;
+            for (int s = 0; s < nsegs; ++s) v += __ldcg(part + (size_t)s * (kTok * kRows) + i);
+            if (bias) v += to_f32(bias[n]);
+            y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v);
+          }
+          if (tc == 0) *counter = 0;
+        }
+      }
+      consumer_sync();  // everyone is done with red[] and s_flag
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+#pragma unroll
+      for (int i = 0; i < kMT; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+    }
+  }
+  (void)ok;
+}
+
+}  // namespace smallm
+
+// ---------------------------------------------------------------------------
+// host launcher
+// ---------------------------------------------------------------------------
+GFX_DEFINE_STATUS_READER(splitk_device_status)
+
+struct SmallMPlan {
+  int nt, tok, tok_blocks, RB, KS, G, max_segs, ctas_per_sm, stages;
+};
+
+static int nt_for(int M) { return M <= 8 ? 1 : (M <= 16 ? 2 : 4); }
+
+static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool f16) {
+  SmallMPlan p{};
+  p.nt = nt_for(M);
+  p.tok = 8 * p.nt;
+  p.tok_blocks = (M + p.tok - 1) / p.tok;
+  p.RB = (N + smallm::kRows - 1) / smallm::kRows;
+  p.KS = (K + smallm::kStageK - 1) / smallm::kStageK;
+  // resident CTAs per SM follow the stage ring + reduction buffer size
+  p.ctas_per_sm = p.nt == 4 ? 1 : 2;
+  p.stages = p.nt == 4 ? 6 : ((!f16 && p.nt == 2) ? 3 : 4);
+  const long long U = (long long)p.RB * p.KS;
+  long long G;
+  if (splits_req > 0) {
+    const int s = splits_req > p.KS ? p.KS : splits_req;
+    G = (long long)p.RB * s;  // classic split-K as a special case of the unit partition
+  } else {
+    G = (long long)sms * p.ctas_per_sm / p.tok_blocks;
+    if (G < 1) G = 1;
+    if (G > U) G = U;
+  }
+  p.G = (int)G;
+  // segments per row block: a row block spans KS units and every CTA range
+  // holds at least floor(U / G) of them
+  const long long min_units = U / G;
+  p.max_segs = (int)((p.KS + min_units - 1) / min_units) + 1;
+  return p;
+}
+
+size_t splitk_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  // sized for the larger of the fp16 / fp32 scale plans
+  size_t need = 0;
+  for (int f = 0; f < 2; ++f) {
+    SmallMPlan p = smallm_plan(M, N, K, splits_req, sms, f == 1);
+    const size_t part = (size_t)p.tok_blocks * p.RB * p.max_segs * p.tok * smallm::kRows * sizeof(float);
+    const size_t b = kSplitKCounterBytes + align_up(part, 256);
+    need = b > need ? b : need;
+  }
+  return need;
+}
+
+int splitk_auto_splits(int M, int N, int K, int sms) {
+  SmallMPlan p = smallm_plan(M, N, K, 0, sms, true);
+  return (p.G + p.RB - 1) / p.RB;
+}
+
+struct SmallMArgs {
+  CUtensorMap nib_map, x_map, scale_map;
+  int scale_tma;
+  const void* ws;
+  const void* bias;
+  void* y;
+  float* part;
+  int* cnt;
+  int M, N, K;
+};
+
+template <int NT, int STAGES, bool F16S, typename OutT>
+static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st) {
+  using L = smallm::Layout<NT, STAGES, F16S>;
+  auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT>;
+  static bool attr_set[64] = {false};  // per device
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess)
+      return set_error(GFX_ERR_CUDA, "w4a16_smallm: cannot set %d bytes of shared memory: %s", L::kSmemBytes,
+                       cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  dim3 grid(p.G, p.tok_blocks);
+  kern<<<grid, smallm::kThreads, L::kSmemBytes, st>>>(a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
+                                                     (const OutT*)a.bias, (OutT*)a.y, a.part, a.cnt, a.M, a.N, a.K,
+                                                     p.G, p.max_segs);
+  return check_launch("w4a16_smallm_kernel");
+}
+
+template <int NT, int STAGES, bool F16S>
+static int launch_smallm_out(int out_dtype, const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st) {
+  if (out_dtype == GFX_DTYPE_F32) return launch_smallm_t<NT, STAGES, F16S, float>(p, a, st);
+  if (out_dtype == GFX_DTYPE_F16) return launch_smallm_t<NT, STAGES, F16S, __half>(p, a, st);
+  return launch_smallm_t<NT, STAGES, F16S, __nv_bfloat16>(p, a, st);
+}
+
+int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+                        int out_dtype, int M, int N, int K, int splits_req, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream, int sms) {
+  const bool f16 = scale_dtype == GFX_SCALE_F16;
+  if (M > 64)
+    return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm: the small-M kernel takes M <= 64 (got M=%d); "
+                     "use splits=0 so larger M runs on the tensor-core kernel", M);
+  SmallMPlan p = smallm_plan(M, N, K, splits_req, sms, f16);
+  SmallMArgs a{};
+  const size_t need = splitk_workspace_bytes(M, N, K, splits_req, sms);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(GFX_ERR_WORKSPACE, "w4a16_gemm: workspace of %zu bytes required, got %zu (ptr %p)", need,
+                     workspace_bytes, workspace);
+  if ((size_t)p.tok_blocks * p.RB * sizeof(int) > kSplitKCounterBytes)
+    return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm: %d x %d row blocks exceed the %zu-byte counter region",
+                     p.tok_blocks, p.RB, kSplitKCounterBytes);
+  // Counters live at a fixed offset (the first kSplitKCounterBytes) so that
+  // calls of any shape sharing one workspace always find them re-armed to
+  // zero; the fp32 partials follow and need no initial value.
+  a.cnt = reinterpret_cast<int*>(workspace);
+  a.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kSplitKCounterBytes);
+  int rc = make_tmap_2d(&a.nib_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                        smallm::kStageBytesPerRow, smallm::kRows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&a.x_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
+                    (uint32_t)p.tok, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const uint64_t elem = f16 ? 2 : 4;
+  const uint64_t groups = (uint64_t)K / 32;
+  a.scale_tma = ((groups * elem) % 16 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) ? 1 : 0;
+  if (a.scale_tma) {
+    rc = make_tmap_2d(&a.scale_map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws,
+                      groups, (uint64_t)N, groups * elem, smallm::kGroupsPerStage, smallm::kRows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    memset(&a.scale_map, 0, sizeof(a.scale_map));
+  }
+  a.ws = ws;
+  a.bias = bias;
+  a.y = y;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  // stage counts: two resident CTAs per SM for NT <= 2 (<= ~110 KB each), one for NT = 4
+  if (f16) {
+    if (p.nt == 1) return launch_smallm_out<1, 4, true>(out_dtype, p, a, stream);
+    if (p.nt == 2) return launch_smallm_out<2, 4, true>(out_dtype, p, a, stream);
+    return launch_smallm_out<4, 6, true>(out_dtype, p, a, stream);
+  }
+  if (p.nt == 1) return launch_smallm_out<1, 4, false>(out_dtype, p, a, stream);
+  if (p.nt == 2) return launch_smallm_out<2, 3, false>(out_dtype, p, a, stream);
+  return launch_smallm_out<4, 6, false>(out_dtype, p, a, stream);
+}
+
+}  // namespace gfx

@@ -201,14 +201,17 @@ def test_gemm_large_m_bias(cuda, out_dtype):
     _check(y.float().cpu().numpy(), O.w4a16_matmul(xn, p, s, bias.float().numpy()))
 
 
-def test_gemm_large_m_matches_splitk_path(cuda):
-    # splits=1 forces the split-K kernel; both paths agree within the bf16 weight rounding
+def test_gemm_large_m_matches_small_m_path(cuda):
+    # the tcgen05 kernel (M=512) and the small-M kernel (the same first 64 rows)
+    # agree within the bf16 rounding of the tensor-core weight operand
     N, K, M = 640, 2048, 512
     p, s, pd, sd = _weights(N, K, 51, cuda)
     _, xd = _x(M, K, 52, cuda)
     a = ops.gemm_w4a16(xd, pd, sd, None, torch.float32).cpu().numpy()
-    b = ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=1).cpu().numpy()
-    _check(a, b)
+    b = ops.gemm_w4a16(xd[:64].contiguous(), pd, sd, None, torch.float32, splits=1).cpu().numpy()
+    _check(a[:64], b)
+    assert ops.gemm_w4a16(xd, pd, sd, None, torch.float32, splits=3).equal(
+        ops.gemm_w4a16(xd, pd, sd, None, torch.float32))  # splits does not change the M > 64 result
 
 
 def test_gemm_large_m_deterministic(cuda):
