@@ -296,6 +296,24 @@ def run_ours(args, world, rank, local):
             del g
         del copies
 
+    # --- int8 weights: the six shapes at M=4608, per-channel fp16 scales ---
+    int8 = None
+    if not args.no_int8:
+        w8 = []
+        for i, (name, K, N, _, _) in enumerate(weights):
+            q, sc = synthetic.int8_weight(N, K, seed=5000 + i)
+            w8.append((q.to(dev), sc.to(dev)))
+
+        def step8():
+            for (q, sc), x in zip(w8, xs):
+                ops.gemm_w8a16(x, q, sc, None, torch.bfloat16)
+        ms8 = max_over_ranks(time_steps(step8, args.steps, args.warmup, world, dev, stream), world, dev)
+        ms8 /= args.steps
+        int8 = {"value": world * flops_step / (ms8 * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms8,
+                "weights": "int8 ~round(N(0,40)) clipped to +-127, one fp16 scale per output channel",
+                "frac_of_sustained_peak": (flops_step / (ms8 * 1e-3) / 1e12) / pk["bf16_tflops_sustained"]}
+        del w8
+
     # --- e2e: public API with host buffers, H2D of x and D2H of y inside the timed region ---
     e2e = None
     if not args.no_e2e:
@@ -339,10 +357,55 @@ def run_ours(args, world, rank, local):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_kind": f"bf16 dense sustained ({pk['source']})",
                          "frac_of_burst": achieved / pk["bf16_tflops"], "traffic": traffic},
-            "cpu_baseline": cpu, "e2e": e2e, "small_m": small,
+            "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8,
             "gpu_launches": args.steps * len(weights), "clocks": clocks.summary(),
         }
         print(json.dumps(out))
+
+
+def run_dit(args, world, rank, local):
+    """the full Flux-architecture DiT forward (random int4
+    weights), batch split or token-row split across the ranks."""
+    from comfy_ui_gfx906_tools_b200 import flux_dit, ops, parallel
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    cfg = flux_dit.DiTConfig()
+    model = flux_dit.FluxDiT(cfg, flux_dit.int4_linear_factory(dev, seed=11), dev)  # same seed: identical replicas
+    side = args.res // 16
+    split = args.split if world > 1 else "none"
+    batch = args.batch if args.batch else (8 if split == "batch" else 1)
+    inputs = flux_dit.make_inputs(cfg, batch, side, side, 512, dev, seed=12)
+    macs = {"n": 0}
+
+    def count(mod, inp, out):
+        macs["n"] += inp[0].numel() // inp[0].shape[-1] * mod.in_features * mod.out_features
+    hooks = [m.register_forward_hook(count) for m in model.modules() if isinstance(m, ops.Gfx906Int4Ops.Linear)]
+
+    def fwd():
+        with torch.no_grad():
+            if split == "batch":
+                return parallel.split_forward_batch(model, *inputs, gather_output=False)
+            if split == "rows":
+                return parallel.split_forward_rows(model, *inputs, side, side, gather_output=False)
+            return model(*inputs)
+    fwd()
+    torch.cuda.synchronize(dev)
+    linear_flop = 2.0 * macs["n"]  # this rank's int4-linear work per forward
+    for h in hooks:
+        h.remove()
+    ms = max_over_ranks(time_steps(fwd, args.steps, args.warmup, world, dev, stream), world, dev) / args.steps
+    tokens = batch * (side * side + 512)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Flux DiT forward tokens/s (int4 linears)", "value": tokens / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random int4 weights)",
+            "config": {"workload": f"flux_dit_{args.res}", "batch": batch, "image_tokens": side * side,
+                       "text_tokens": 512, "split": split, "blocks": "19 double + 38 single, hidden 3072"},
+            "linear_tflops_per_gpu": linear_flop / (ms * 1e-3) / 1e12,
+        }))
 
 
 def main():
@@ -355,6 +418,11 @@ def main():
     ap.add_argument("--no-small", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-int8", action="store_true")
+    ap.add_argument("--workload", choices=["gemm", "dit"], default="gemm")
+    ap.add_argument("--res", type=int, default=1024, help="dit: latent resolution in pixels (1024 or 2048)")
+    ap.add_argument("--split", choices=["batch", "rows"], default="batch", help="dit: how N > 1 ranks split")
+    ap.add_argument("--batch", type=int, default=0, help="dit: batch (default 8 for the batch split, else 1)")
     args = ap.parse_args()
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -363,7 +431,10 @@ def main():
         return
     world, rank, local = setup_dist(args.gpus)
     try:
-        run_ours(args, world, rank, local)
+        if args.workload == "dit":
+            run_dit(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -166,9 +166,18 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
 int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,
                const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
                size_t workspace_bytes, gfx_stream_t stream) {
-  (void)x; (void)x_dtype; (void)w_q8; (void)w_scale; (void)scale_per_channel; (void)bias; (void)y;
-  (void)out_dtype; (void)M; (void)N; (void)K; (void)splits; (void)workspace; (void)workspace_bytes; (void)stream;
-  return set_error(GFX_ERR_UNSUPPORTED, "w8a16_gemm: not built yet");
+  (void)workspace;
+  (void)workspace_bytes;
+  int rc = check_gemm_common("w8a16_gemm", x, x_dtype, w_q8, w_scale, GFX_SCALE_F32, y, out_dtype, M, N, K, splits);
+  if (rc) return rc;
+  if (scale_per_channel != 0 && scale_per_channel != 1)
+    return set_error(GFX_ERR_INVALID, "w8a16_gemm: scale_per_channel must be 0 or 1, got %d", scale_per_channel);
+  if (scale_per_channel && (reinterpret_cast<uintptr_t>(w_scale) & 1))
+    return set_error(GFX_ERR_INVALID, "w8a16_gemm: float16 channel scales must be 2-byte aligned");
+  if (M == 0) return GFX_OK;
+  // Every M runs on the tensor-core kernel (the int8 path has no small-M kernel yet).
+  return launch_w8a16_tc(x, w_q8, w_scale, scale_per_channel, bias, y, out_dtype, M, N, K,
+                         reinterpret_cast<cudaStream_t>(stream), sm_count(current_device()));
 }
 
 size_t w8a16_workspace_bytes(int M, int N, int K, int splits) {

@@ -23,11 +23,13 @@ size_t splitk_workspace_bytes(int M, int N, int K, int splits, int sms);
 int splitk_auto_splits(int M, int N, int K, int sms);
 int splitk_device_status(int clear);
 
-// W4A16, large M (tcgen05 + TMEM, persistent) -- w4a16_tc.cu
+// W4A16 / W8A16, large M (tcgen05 + TMEM, persistent) -- w4a16_tc.cu
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 bool w4a16_tc_supported(int M, int N, int K, int scale_dtype);
 int tc_device_status(int clear);
+int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 
 // loaders / helpers -- pack.cu
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,

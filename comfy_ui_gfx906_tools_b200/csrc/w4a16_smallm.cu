@@ -17,26 +17,34 @@
 //    scales (TMA when the scale row stride is 16-byte aligned, else cp.async)
 //    and the matching 256-wide slice of the activations (TMA, SWIZZLE_128B
 //    boxes) into a shared-memory ring.
-//  * Eight consumer warps = 4 row slices (32 rows) x 2 K halves (4 of the 8
-//    32-groups of a unit). A warp reads one 32-bit nibble word per row with
-//    ldmatrix (conflict-free through the swizzle), turns nibbles into EXACT
-//    bf16 integer codes with one LOP3 + one bf16x2 FMA per pair (magic
-//    0x4300|u = 128+u), and runs mma.sync m16n8k16 with the weights as the
-//    16-row A operand and the tokens as the 8-column B operand. Each MMA pair
-//    covers exactly one 32-group, so its fp32 partial is scaled in registers
-//    (acc += partial * scale): the result is the fp32 dequant-then-matmul up
-//    to fp32 rounding (the weight operand is never rounded to bf16).
-//  * When a CTA leaves a row block (segment end) the two K halves are summed
+//  * Eight consumer warps = 2 row slices (64 rows, 4 m16 tiles) x 4 K quarters
+//    (one pair of 32-groups of the unit each), so one activation fragment feeds
+//    64 weight rows. A warp reads one 32-bit nibble word per row and group
+//    with ldmatrix (conflict-free through the swizzle) and turns each nibble
+//    pair into bf16x2 "magic" values 128 + (code + 8) with one LOP3. The MMA
+//    (mma.sync m16n8k16, weights = 16-row A, tokens = 8-column B) multiplies
+//    those exact values; the +136 offset is removed by starting the group's
+//    accumulator at -136 * sum(x) -- one extra MMA with a constant A operand,
+//    shared by the warp's four m16 tiles. Each MMA pair covers exactly one
+//    32-group, so its fp32 partial is scaled in registers (acc += p * scale).
+//    No weight is ever rounded to bf16: products are exact and only the fp32
+//    summation order differs from the fp32 dequant-then-matmul.
+//  * When a CTA leaves a row block (segment end) the K quarters are summed
 //    through shared memory. A row block covered by one CTA is stored directly
 //    (+bias). Otherwise each segment writes its fp32 partial to the workspace
 //    and bumps the row block's arrival counter; the last arrival (no spinning)
 //    sums the segments in segment order -- deterministic -- adds the bias,
 //    stores, and re-arms the counter to zero.
 //
-// K order inside one 16-wide MMA step is permuted (both operands alike) so
-// that each thread's weights come from one nibble word with no byte shuffles:
-// k-slot (2t, 2t+1) of step s holds elements (8t + 2s, 8t + 2s + 4) and slot
-// (2t + 8, 2t + 9) holds (8t + 2s + 1, 8t + 2s + 5) of the 32-group.
+// Two index permutations keep every operand load a single instruction:
+//  * K inside a 16-wide MMA step (both operands alike): k-slot (2t, 2t+1) of
+//    step s holds group elements (8t + 2s, 8t + 2s + 4), slot (2t + 8, 2t + 9)
+//    holds (8t + 2s + 1, 8t + 2s + 5) -- each A register is two nibbles of one
+//    word, each B register two 16-bit halves of one 16-byte activation load.
+//  * MMA column n reads token pi(n) = (n >> 1) | ((n & 1) << 2) of its 8-token
+//    tile, so the two token rows a quarter-warp reads differ in swizzle bit 2
+//    and the 16-byte activation loads are bank-conflict free; the epilogue
+//    maps columns back through the same pi.
 #include <cstring>
 
 #include "common.cuh"
@@ -48,15 +56,22 @@ namespace smallm {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kRows = 128;                      // weight rows per unit (4 slices x 32)
+constexpr int kRows = 128;                      // weight rows per unit
 constexpr int kStageK = 256;                    // K per unit
 constexpr int kStageBytesPerRow = kStageK / 2;  // 128 nibble bytes = one SW128 row
 constexpr int kGroupsPerStage = kStageK / 32;
-constexpr int kMT = 2;                          // m16 tiles per warp (32 rows)
 constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 consumer threads
 
+// Warp tiling: kMT m16 tiles per warp (rows), the 8 consumer warps split into
+// kRowSlices row slices x kKParts K parts (each K part owns kGPW of the 8
+// groups of a unit). More m16 tiles per warp amortise the activation
+// fragments; fewer keep the accumulators of larger token tiles in registers.
 template <int NT, int STAGES, bool kF16Scale>
 struct Layout {
+  static constexpr int kMT = NT == 1 ? 4 : 2;
+  static constexpr int kRowSlices = kRows / (16 * kMT);
+  static constexpr int kKParts = kConsumerWarps / kRowSlices;
+  static constexpr int kGPW = kGroupsPerStage / kKParts;  // groups per warp per unit (even)
   static constexpr int kTok = 8 * NT;
   static constexpr int kNibBytes = kRows * kStageBytesPerRow;
   static constexpr int kScaleRowBytes = kGroupsPerStage * (kF16Scale ? 2 : 4);  // dense [row][group]
@@ -65,15 +80,13 @@ struct Layout {
   static constexpr int kXBytes = (4 * kXBoxBytes + 1023) / 1024 * 1024;
   static constexpr int kStageBytes = kNibBytes + kScaleBytes + kXBytes;
   static constexpr int kAcc = kMT * NT * 4;      // accumulators per thread
-  static constexpr int kRedBytes = 4 * 32 * kAcc * 4;  // K-half reduction, aliases a stage's nibbles
-  static_assert(kRedBytes <= kNibBytes, "reduction buffer must fit in a stage's nibble tile");
+  static constexpr int kRedBytes = kRowSlices * 32 * kAcc * 4;  // one K quarter, aliases the held stage
+  static_assert(kRedBytes <= kStageBytes, "a K quarter's reduction buffer must fit in one stage");
   static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + 2 * STAGES * 8 + 64;
 };
 
-__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+__device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -85,18 +98,20 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
 
-// Two nibbles (at bit 0 and bit 16 of w_shifted) -> bf16x2 exact integer codes.
-__device__ __forceinline__ uint32_t nib_pair_to_bf16x2(uint32_t w_shifted) {
-  // (w & 0x000F000F) ^ 0x43084308 == 0x4300 | (nib ^ 8) per half: 128 + u, u = code + 8
-  const uint32_t magic = and_xor(w_shifted, 0x000F000Fu, 0x43084308u);
-  uint32_t c;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(c) : "r"(magic), "r"(0x3F803F80u), "r"(0xC308C308u));  // -136, exact
-  return c;
+// Nibbles at bit 0 and bit 16 of w_shifted -> bf16x2 (128 + u) with u = nib ^ 8
+// = code + 8: (w & 0x000F000F) ^ 0x43084308 == 0x4300 | (nib ^ 8) per half.
+__device__ __forceinline__ uint32_t nib_pair_magic(uint32_t w_shifted) {
+  return and_xor(w_shifted, 0x000F000Fu, 0x43084308u);
 }
+
+constexpr uint32_t kMinus136x2 = 0xC308C308u;  // bf16x2 (-136, -136)
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumerWarps * 32) : "memory");
 }
+
+// Token row of MMA column n within an 8-token tile (conflict-free activation loads).
+__device__ __forceinline__ int tok_perm(int n) { return (n >> 1) | ((n & 1) << 2); }
 
 // First CTA whose unit range contains unit t: largest c with floor(c*U/G) <= t.
 __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
@@ -104,7 +119,7 @@ __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
 }
 
 template <int NT, int STAGES, bool kF16Scale, typename OutT>
-__global__ void __launch_bounds__(kThreads) w4a16_smallm_kernel(
+__global__ void __launch_bounds__(kThreads, NT <= 2 ? 2 : 1) w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
     const OutT* __restrict__ bias, OutT* __restrict__ y, float* __restrict__ partials, int* __restrict__ counters,
@@ -140,7 +155,6 @@ __global__ void __launch_bounds__(kThreads) w4a16_smallm_kernel(
   __syncthreads();
   if (n_iters <= 0) return;
 
-  bool ok = true;
   if (warp == kConsumerWarps) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
@@ -151,7 +165,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_smallm_kernel(
     for (int it = 0; it < n_iters; ++it) {
       const int stage = it % STAGES;
       const uint32_t phase = (it / STAGES) & 1;
-      if (!mbar_wait(&empty[stage], phase ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+      if (!mbar_wait(&empty[stage], phase ^ 1, kDevErrEmptyBarrierTimeout)) break;
       const long long u = u_begin + it;
       const int rb = (int)(u / KS), ks = (int)(u % KS);
       uint8_t* st = smem + stage * L::kStageBytes;
@@ -181,192 +195,230 @@ __global__ void __launch_bounds__(kThreads) w4a16_smallm_kernel(
         cp_async_mbar_arrive_noinc(&full[stage]);
       }
     }
-  } else {
-    // ------------------------------ consumers -----------------------------
-    const int rs = warp & 3;   // row slice: rows rs*32 .. rs*32+31 of the row block
-    const int kh = warp >> 2;  // K half: groups 4*kh .. 4*kh+3 of each unit
-    const int g_ = lane >> 2, t_ = lane & 3;
-    const int lm_i = lane >> 3, lm_j = lane & 7;
-    float acc[kMT][NT][4];
+    return;
+  }
+
+  // ------------------------------ consumers -----------------------------
+  constexpr int kMT = L::kMT, kRowSlices = L::kRowSlices, kKParts = L::kKParts, kGPW = L::kGPW;
+  const int rs = warp % kRowSlices;  // row slice: rows rs*16*kMT .. of the row block
+  const int kq = warp / kRowSlices;  // K part: groups kq*kGPW .. kq*kGPW + kGPW - 1 of each unit
+  const int g_ = lane >> 2, t_ = lane & 3;
+  const int lm_j = lane & 7, lm_hi = (lane >> 3) & 1;  // ldmatrix.x2: matrix (lane>>3)&1, row lane&7
+  const int xrow_in_tile = tok_perm(g_);
+  float acc[kMT][NT][4];
+#pragma unroll
+  for (int i = 0; i < kMT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+
+  for (int it = 0; it < n_iters; ++it) {
+    const int stage = it % STAGES;
+    const uint32_t phase = (it / STAGES) & 1;
+    // A consumer that gives up here leaves early; its peers reach the same
+    // wait (they all consume the same stages) and give up the same way.
+    if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) return;
+    const uint8_t* st = smem + stage * L::kStageBytes;
+    const uint32_t nib_base = smem_u32(st);
+    const uint8_t* sc = st + L::kNibBytes;
+#pragma unroll
+    for (int gi = 0; gi < kGPW; ++gi) {
+      const int grp = kq * kGPW + gi;
+      const int h = grp & 1;  // which 32-group of x box grp/2
+      const uint8_t* xs = sc + L::kScaleBytes + (grp >> 1) * L::kXBoxBytes;
+      // B fragments (activations) of this group for each token tile, and the
+      // offset correction p0 = -136 * sum_k x (constant A operand).
+      uint32_t b[NT][4];
+      float p0[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int row = nt * 8 + xrow_in_tile;
+        const int chunk = h * 4 + t_;
+        const uint4 v = *reinterpret_cast<const uint4*>(xs + row * 128 + ((chunk ^ (row & 7)) << 4));
+        b[nt][0] = prmt(v.x, v.z, 0x5410);  // step 0, slots (2t, 2t+1)
+        b[nt][1] = prmt(v.x, v.z, 0x7632);  // step 0, slots (2t+8, 2t+9)
+        b[nt][2] = prmt(v.y, v.w, 0x5410);  // step 1
+        b[nt][3] = prmt(v.y, v.w, 0x7632);
+        const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_bf16_16816(p0[nt], kMinus136x2, kMinus136x2, kMinus136x2, kMinus136x2, b[nt][0], b[nt][1], zero);
+        mma_bf16_16816(p0[nt], kMinus136x2, kMinus136x2, kMinus136x2, kMinus136x2, b[nt][2], b[nt][3], p0[nt]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < kMT; ++mt) {
+        const int rbase = rs * 16 * kMT + mt * 16;
+        // word t of group grp for rows rbase+g (matrix 0) and rbase+8+g (matrix 1)
+        const int lrow = rbase + lm_j + lm_hi * 8;
+        uint32_t wr, wr8;
+        ldmatrix_x2(nib_base + lrow * kStageBytesPerRow + ((grp ^ (lrow & 7)) << 4), wr, wr8);
+        const int r_lo = rbase + g_, r_hi = r_lo + 8;
+        float s_r, s_r8;
+        if (kF16Scale) {
+          const __half* sch = reinterpret_cast<const __half*>(sc);
+          s_r = __half2float(sch[r_lo * kGroupsPerStage + grp]);
+          s_r8 = __half2float(sch[r_hi * kGroupsPerStage + grp]);
+        } else {
+          const float* scf = reinterpret_cast<const float*>(sc);
+          s_r = scf[r_lo * kGroupsPerStage + grp];
+          s_r8 = scf[r_hi * kGroupsPerStage + grp];
+        }
+        // step 0: slots (2t,2t+1) <- (n0,n4), (2t+8,2t+9) <- (n1,n5)
+        // step 1: slots (2t,2t+1) <- (n2,n6), (2t+8,2t+9) <- (n3,n7)
+        const uint32_t a00 = nib_pair_magic(wr), a01 = nib_pair_magic(wr8);
+        const uint32_t a02 = nib_pair_magic(wr >> 4), a03 = nib_pair_magic(wr8 >> 4);
+        const uint32_t a10 = nib_pair_magic(wr >> 8), a11 = nib_pair_magic(wr8 >> 8);
+        const uint32_t a12 = nib_pair_magic(wr >> 12), a13 = nib_pair_magic(wr8 >> 12);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float p[4];
+          mma_bf16_16816(p, a00, a01, a02, a03, b[nt][0], b[nt][1], p0[nt]);
+          mma_bf16_16816(p, a10, a11, a12, a13, b[nt][2], b[nt][3], p);
+          acc[mt][nt][0] = fmaf(p[0], s_r, acc[mt][nt][0]);
+          acc[mt][nt][1] = fmaf(p[1], s_r, acc[mt][nt][1]);
+          acc[mt][nt][2] = fmaf(p[2], s_r8, acc[mt][nt][2]);
+          acc[mt][nt][3] = fmaf(p[3], s_r8, acc[mt][nt][3]);
+        }
+      }
+    }
+
+    // ---------------- segment end: leaving a row block (or the range) ----------------
+    const long long u = u_begin + it;
+    const bool seg_end = (((u + 1) % KS) == 0) || (it == n_iters - 1);
+    if (!seg_end) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      continue;
+    }
+    const int rb = (int)(u / KS);
+    const long long rb_lo = (long long)rb * KS, rb_hi = rb_lo + KS;
+    const long long seg_lo = u_begin > rb_lo ? u_begin : rb_lo;
+    const bool single = (seg_lo == rb_lo) && (u + 1 == rb_hi);
+    // The stage is still held (not yet released to the producer), so once
+    // every consumer is done reading it, it doubles as the reduction buffer.
+    // Layout [quarter-1][element][slice*32 + lane]: consecutive lanes write
+    // consecutive words (no bank conflicts).
+    float* red = reinterpret_cast<float*>(const_cast<uint8_t*>(st));
+    constexpr int kRedStride = kRowSlices * 32;                     // floats per element row
+    constexpr int kRedQuarter = L::kAcc * kRedStride;               // floats per K quarter
+    constexpr bool kOneRound = (kKParts - 1) * kRedQuarter * 4 <= L::kStageBytes;
+    const int rl = rs * 32 + lane;
+    consumer_sync();
+    // 1) K parts 1.. -> part 0
+    if (kOneRound) {
+      if (kq != 0) {
+        float* dst = red + (kq - 1) * kRedQuarter + rl;
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[((mt * NT + nt) * 4 + e) * kRedStride] = acc[mt][nt][e];
+      }
+      consumer_sync();
+      if (kq == 0) {
+#pragma unroll
+        for (int q = 0; q < kKParts - 1; ++q) {
+          const float* src = red + q * kRedQuarter + rl;
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[mt][nt][e] += src[((mt * NT + nt) * 4 + e) * kRedStride];
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int q = 1; q < kKParts; ++q) {
+        if (kq == q) {
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) red[((mt * NT + nt) * 4 + e) * kRedStride + rl] = acc[mt][nt][e];
+        }
+        consumer_sync();
+        if (kq == 0) {
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[mt][nt][e] += red[((mt * NT + nt) * 4 + e) * kRedStride + rl];
+        }
+        consumer_sync();
+      }
+    }
+    const int n0 = rb * kRows;
+    if (single) {
+      if (kq == 0) {
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int n = n0 + rs * 16 * kMT + mt * 16 + g_ + half * 8;
+            if (n >= N) continue;
+            const float bv = bias ? to_f32(bias[n]) : 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int cc = 0; cc < 2; ++cc) {
+                const int tok = tok0 + nt * 8 + tok_perm(2 * t_ + cc);
+                if (tok < M) y[(size_t)tok * N + n] = from_f32<OutT>(acc[mt][nt][half * 2 + cc] + bv);
+              }
+          }
+      }
+    } else {
+      // 2) this segment's partial -> workspace slot [tb][rb][seg] ([token][row] order)
+      const int seg = c - owner_cta(rb_lo, U, G);
+      float* part = partials + (((size_t)tb * RB + rb) * max_segs) * (kTok * kRows);
+      if (kq == 0) {
+        float* mine = part + (size_t)seg * (kTok * kRows);
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int r = rs * 16 * kMT + mt * 16 + g_ + half * 8;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int cc = 0; cc < 2; ++cc)
+                mine[(nt * 8 + tok_perm(2 * t_ + cc)) * kRows + r] = acc[mt][nt][half * 2 + cc];
+          }
+        __threadfence();
+      }
+      consumer_sync();
+      int* counter = counters + (size_t)tb * RB + rb;
+      const int nsegs = owner_cta(rb_hi - 1, U, G) - owner_cta(rb_lo, U, G) + 1;
+      if (warp == 0 && lane == 0) *s_flag = (atomicAdd(counter, 1) == nsegs - 1);
+      consumer_sync();
+      if (*s_flag) {
+        __threadfence();
+        // 3) last arrival: fixed-order sum over the segments, + bias, store, re-arm
+        const int tc = threadIdx.x;  // 0..255 (consumers)
+        for (int i = tc; i < kTok * kRows; i += kConsumerWarps * 32) {
+          const int tok = i / kRows, r = i % kRows;
+          const int n = n0 + r;
+          if (n >= N || tok0 + tok >= M) continue;
+          float v = 0.0f;
+          for (int s = 0; s < nsegs; ++s) v += __ldcg(part + (size_t)s * (kTok * kRows) + i);
+          if (bias) v += to_f32(bias[n]);
+          y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v);
+        }
+        if (tc == 0) *counter = 0;
+      }
+    }
+    consumer_sync();  // everyone is done with the held stage and s_flag
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
 #pragma unroll
     for (int i = 0; i < kMT; ++i)
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
-
-    for (int it = 0; it < n_iters; ++it) {
-      const int stage = it % STAGES;
-      const uint32_t phase = (it / STAGES) & 1;
-      if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) { ok = false; break; }
-      const uint8_t* st = smem + stage * L::kStageBytes;
-      const uint32_t nib_base = smem_u32(st);
-      const uint8_t* sc = st + L::kNibBytes;
-      const uint8_t* xs = sc + L::kScaleBytes;
-#pragma unroll
-      for (int pp = 0; pp < 2; ++pp) {
-        const int gp = 4 * kh + 2 * pp;  // group pair (gp, gp+1), x box gp/2
-        uint32_t xf[2][NT][4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const int tok = nt * 8 + g_;
-            const int chunk = h * 4 + t_;
-            const uint4 v = *reinterpret_cast<const uint4*>(xs + (gp >> 1) * L::kXBoxBytes + tok * 128 +
-                                                            ((chunk ^ (tok & 7)) << 4));
-            xf[h][nt][0] = v.x; xf[h][nt][1] = v.y; xf[h][nt][2] = v.z; xf[h][nt][3] = v.w;
-          }
-        }
-        uint32_t w[kMT][4];
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt) {
-          const int lrow = rs * 32 + mt * 16 + lm_j + (lm_i & 1) * 8;
-          const int lgrp = gp + (lm_i >> 1);
-          ldmatrix_x4(nib_base + lrow * kStageBytesPerRow + ((lgrp ^ (lrow & 7)) << 4), w[mt][0], w[mt][1],
-                      w[mt][2], w[mt][3]);
-        }
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t wr = w[mt][2 * h], wr8 = w[mt][2 * h + 1];
-            const int r_lo = rs * 32 + mt * 16 + g_, r_hi = r_lo + 8;
-            float s_r, s_r8;
-            if (kF16Scale) {
-              const __half* sch = reinterpret_cast<const __half*>(sc);
-              s_r = __half2float(sch[r_lo * kGroupsPerStage + gp + h]);
-              s_r8 = __half2float(sch[r_hi * kGroupsPerStage + gp + h]);
-            } else {
-              const float* scf = reinterpret_cast<const float*>(sc);
-              s_r = scf[r_lo * kGroupsPerStage + gp + h];
-              s_r8 = scf[r_hi * kGroupsPerStage + gp + h];
-            }
-            const uint32_t a00 = nib_pair_to_bf16x2(wr), a01 = nib_pair_to_bf16x2(wr8);
-            const uint32_t a02 = nib_pair_to_bf16x2(wr >> 4), a03 = nib_pair_to_bf16x2(wr8 >> 4);
-            const uint32_t a10 = nib_pair_to_bf16x2(wr >> 8), a11 = nib_pair_to_bf16x2(wr8 >> 8);
-            const uint32_t a12 = nib_pair_to_bf16x2(wr >> 12), a13 = nib_pair_to_bf16x2(wr8 >> 12);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const uint32_t* xv = xf[h][nt];
-              const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-              float p[4];
-              mma_bf16_16816(p, a00, a01, a02, a03, prmt(xv[0], xv[2], 0x5410), prmt(xv[0], xv[2], 0x7632), zero);
-              mma_bf16_16816(p, a10, a11, a12, a13, prmt(xv[1], xv[3], 0x5410), prmt(xv[1], xv[3], 0x7632), p);
-              acc[mt][nt][0] = fmaf(p[0], s_r, acc[mt][nt][0]);
-              acc[mt][nt][1] = fmaf(p[1], s_r, acc[mt][nt][1]);
-              acc[mt][nt][2] = fmaf(p[2], s_r8, acc[mt][nt][2]);
-              acc[mt][nt][3] = fmaf(p[3], s_r8, acc[mt][nt][3]);
-            }
-          }
-        }
-      }
-      // ---------------- segment end: leaving a row block (or the range) ----------------
-      const long long u = u_begin + it;
-      const bool seg_end = (((u + 1) % KS) == 0) || (it == n_iters - 1);
-      if (!seg_end) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        continue;
-      }
-      const int rb = (int)(u / KS);
-      const long long rb_lo = (long long)rb * KS, rb_hi = rb_lo + KS;
-      const long long seg_lo = u_begin > rb_lo ? u_begin : rb_lo;
-      const bool single = (seg_lo == rb_lo) && (u + 1 == rb_hi);
-      // The stage is still held (not yet released to the producer): its
-      // nibble tile doubles as the K-half reduction buffer once every
-      // consumer is done reading it.
-      float* red = reinterpret_cast<float*>(const_cast<uint8_t*>(st));
-      consumer_sync();
-      // 1) K halves -> kh 0 (through shared memory)
-      float* my_red = red + (rs * 32 + lane) * L::kAcc;
-      if (kh == 1) {
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) my_red[(mt * NT + nt) * 4 + e] = acc[mt][nt][e];
-      }
-      consumer_sync();
-      if (kh == 0) {
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[mt][nt][e] += my_red[(mt * NT + nt) * 4 + e];
-      }
-      const int n0 = rb * kRows;
-      if (single) {
-        if (kh == 0) {
-#pragma unroll
-          for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              const int n = n0 + rs * 32 + mt * 16 + g_ + half * 8;
-              if (n >= N) continue;
-              const float b = bias ? to_f32(bias[n]) : 0.0f;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                  const int tok = tok0 + nt * 8 + 2 * t_ + cc;
-                  if (tok < M) y[(size_t)tok * N + n] = from_f32<OutT>(acc[mt][nt][half * 2 + cc] + b);
-                }
-            }
-        }
-      } else {
-        // 2) partial of this segment -> workspace slot [tb][rb][seg]
-        const int seg = c - owner_cta(rb_lo, U, G);
-        float* part = partials + (((size_t)tb * RB + rb) * max_segs) * (kTok * kRows);
-        if (kh == 0) {
-          float* mine = part + (size_t)seg * (kTok * kRows);
-#pragma unroll
-          for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              const int r = rs * 32 + mt * 16 + g_ + half * 8;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) mine[(nt * 8 + 2 * t_ + cc) * kRows + r] = acc[mt][nt][half * 2 + cc];
-            }
-          __threadfence();
-        }
-        consumer_sync();
-        int* counter = counters + (size_t)tb * RB + rb;
-        const int nsegs = owner_cta(rb_hi - 1, U, G) - owner_cta(rb_lo, U, G) + 1;
-        if (warp == 0 && lane == 0) *s_flag = (atomicAdd(counter, 1) == nsegs - 1);
-        consumer_sync();
-        if (*s_flag) {
-          __threadfence();
-          // 3) last arrival: fixed-order sum over the segments, + bias, store, re-arm
-          const int tc = threadIdx.x;  // 0..255 (consumers)
-          for (int i = tc; i < kTok * kRows; i += kConsumerWarps * 32) {
-            const int tok = i / kRows, r = i % kRows;
-            const int n = n0 + r;
-            if (n >= N || tok0 + tok >= M) continue;
-            float v = 0.0f;
-            for (int s = 0; s < nsegs; ++s) v += __ldcg(part + (size_t)s * (kTok * kRows) + i);
-            if (bias) v += to_f32(bias[n]);
-            y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v);
-          }
-          if (tc == 0) *counter = 0;
-        }
-      }
-      consumer_sync();  // everyone is done with red[] and s_flag
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-#pragma unroll
-      for (int i = 0; i < kMT; ++i)
-#pragma unroll
-        for (int j = 0; j < NT; ++j)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
-    }
   }
-  (void)ok;
 }
 
 }  // namespace smallm

@@ -1,12 +1,16 @@
-// W4A16 large-M GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Weight-only GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), large M.
 //
-// y[M, N] = x[M, K] @ bf16(code[N, K] * scale[N, K/32])^T (+ bias)
+// int4: y[M, N] = x[M, K] @ bf16(code[N, K] * scale[N, K/32])^T (+ bias)
+// int8: y[M, N] = x @ bf16(q[N, K] * scale[N, K/32])^T, or, with one scale per
+//       output channel, (x @ q^T) * scale[N] (+ bias)
 //
-// Reference counterpart: int4_gemm_kernel (nodes/ComfyUI-Gfx906Int4/csrc/
-// int4_gemm_scaled.hip:53-180) behind gemm_int4 (binding.cpp:73-112) for the
-// large-M DiT linears. Same weight buffers; the weights are dequantized to the
-// bf16 values the reference's W4A16 emulation multiplies with (nodes.py:43-52),
-// bit for bit, and multiplied on the tensor cores with fp32 accumulation.
+// Reference counterparts: int4_gemm_kernel (nodes/ComfyUI-Gfx906Int4/csrc/
+// int4_gemm_scaled.hip:53-180) behind gemm_int4 (binding.cpp:73-112), and
+// int8_gemm_kernel (csrc/int8_gemm.hip:66-213) behind gemm_int8
+// (binding.cpp:190-217). Same weight buffers; int4 weights are dequantized to
+// the bf16 values the reference's W4A16 emulation multiplies with
+// (nodes.py:43-52), bit for bit, and multiplied on the tensor cores with fp32
+// accumulation.
 //
 // Design (one persistent CTA per SM, 14 warps, swap-AB):
 //   D[n, m] (TMEM, 128 lanes = weight rows, 256 fp32 columns = tokens)
@@ -15,22 +19,25 @@
 //   Putting the 128-row weight tile on the MMA's M side lets one dequantized
 //   weight element feed 256 tokens, which halves the dequant work per FLOP
 //   compared with a 128-token tile.
-//   warp 4      TMA producer: x tile (TMA, 32 KB), nibble tile (TMA, 4 KB,
-//               SWIZZLE_32B) and group scales (cp.async) per 64-wide K stage.
-//   warps 6-13  dequant: each thread turns 32 nibbles of one weight row into
-//               bf16 in the UMMA canonical SW128 layout, then a proxy fence
-//               and an mbarrier arrival hand the stage to the MMA.
+//   warp 4      TMA producer: x tile (TMA, 32 KB), packed weight tile (TMA:
+//               int4 4 KB SWIZZLE_32B, int8 8 KB SWIZZLE_64B) and per-group
+//               scales (cp.async) per 64-wide K stage.
+//   warps 6-13  dequant: each thread turns 32 weights of one row into bf16 in
+//               the UMMA canonical SW128 layout, then a proxy fence and an
+//               mbarrier arrival hand the stage to the MMA.
 //   warp 5      TMEM allocation + one elected thread issuing tcgen05.mma
 //               (M=128, N=256, K=16; 4 per stage) and tcgen05.commit.
 //   warps 0-3   epilogue: tcgen05.ld of the accumulator (warp w owns TMEM
-//               lanes 32w..32w+31), + bias, convert, store. The accumulator
-//               is double-buffered (2 x 256 columns = all 512), so the
-//               epilogue of tile i overlaps the main loop of tile i+1.
-// Exact dequant: with fp16-valued scales the product code*scale is exact in
-// fp32 and one rounding to bf16 equals the reference's two roundings; it is
-// computed as fma.rn.bf16x2(code, s_hi, code * s_lo) with s = s_hi + s_lo
-// split into two bf16 parts (code * s_lo is exact in bf16), 2.5 ops per
-// element. General fp32 scales use an fp32 multiply then one cvt.rn to bf16.
+//               lanes 32w..32w+31), (* channel scale) + bias, convert, store.
+//               The accumulator is double-buffered (2 x 256 columns = all
+//               512), so the epilogue of tile i overlaps the main loop of
+//               tile i+1.
+// Exact int4 dequant: with fp16-valued scales the product code*scale is exact
+// in fp32 and one rounding to bf16 equals the reference's two roundings; it is
+// computed as fma.rn.bf16x2(code, s_hi, code * s_lo) with s = s_hi + s_lo split
+// into two bf16 parts (code * s_lo is exact in bf16), 2.5 ops per element.
+// General fp32 scales use an fp32 multiply then one cvt.rn to bf16. int8 codes
+// are exact in bf16; a per-channel scale is applied to the fp32 accumulator.
 // Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "kernels.h"
@@ -45,19 +52,35 @@ constexpr int kTileN = 128;       // weight rows per tile (MMA M)
 constexpr int kTileM = 256;       // tokens per tile (MMA N)
 constexpr int kStageK = 64;       // K per pipeline stage (one 128-byte swizzle row of bf16)
 constexpr int kUmmaK = 16;
-constexpr int kStages = 4;
 constexpr int kThreads = 14 * 32;
 constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6, kDequantWarps = 8;
 constexpr int kAccCols = kTileM;  // fp32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
-
-constexpr int kXBytes = kTileM * kStageK * 2;       // 32 KB
-constexpr int kWBytes = kTileN * kStageK * 2;       // 16 KB
-constexpr int kNibBytes = kTileN * kStageK / 2;     // 4 KB
-constexpr int kScaleBytes = 1024;                   // 128 rows x 2 groups x 4 B
-constexpr int kStageBytes = kXBytes + kWBytes + kNibBytes + kScaleBytes;
+constexpr int kXBytes = kTileM * kStageK * 2;  // 32 KB
+constexpr int kWBytes = kTileN * kStageK * 2;  // 16 KB
 constexpr int kBarrierBytes = 256;
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+
+// Weight formats.
+enum Fmt : int {
+  kInt4GroupF32 = 0,  // int4 nibbles, fp32 scale per 32-group (the reference's format)
+  kInt4GroupF16 = 1,  // int4 nibbles, fp16-valued scale per 32-group (exact fp16 copy)
+  kInt8GroupF32 = 2,  // int8, fp32 scale per 32-group (the reference's quantize_int8 format)
+  kInt8ChanF16 = 3,   // int8, fp16 scale per output channel
+};
+
+template <int F>
+struct Traits {
+  static constexpr bool kInt8 = F >= kInt8GroupF32;
+  static constexpr bool kChannel = F == kInt8ChanF16;
+  static constexpr bool kF16Group = F == kInt4GroupF16;
+  static constexpr int kQRowBytes = kInt8 ? kStageK : kStageK / 2;  // packed bytes per row per stage
+  static constexpr int kQBytes = kTileN * kQRowBytes;
+  static constexpr int kScaleBytes = kChannel ? 0 : 1024;            // 128 rows x 2 groups x <= 4 B
+  static constexpr int kStageBytes = kXBytes + kWBytes + kQBytes + kScaleBytes;
+  static constexpr int kStages = (1024 + 4 * kStageBytes + kBarrierBytes <= 232448) ? 4 : 3;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+  static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-byte aligned");
+};
 
 // Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M=128, N=256.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileM >> 3) << 17) |
@@ -128,7 +151,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
 
 // One 32-bit nibble word (elements 8j..8j+7 of a row) -> 8 bf16 = 16 bytes.
 template <bool kF16Scale>
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, float s, uint32_t s_hi2, uint32_t s_lo2) {
+__device__ __forceinline__ uint4 dequant_nibble_word(uint32_t w, float s, uint32_t s_hi2, uint32_t s_lo2) {
   uint32_t out[4];
   if constexpr (kF16Scale) {
     const uint32_t t2 = w >> 4;
@@ -154,6 +177,20 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, float s, uint32_t s_hi
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
+// Four int8 weights (one word) -> two bf16x2. Scaled: RN(float(q) * s); else the exact code.
+template <bool kScaled>
+__device__ __forceinline__ uint2 dequant_int8_word(uint32_t w, float s) {
+  const uint32_t xo = w ^ 0x80808080u;  // offset binary u = q + 128
+  float f[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bytes [u_i, 0, 0, 0x4B] -> float 2^23 + u_i, minus 2^23 + 128 -> q_i exactly
+    f[i] = __uint_as_float(prmt(xo, 0x4Bu, 0x4650u + i)) - 8388736.0f;
+    if (kScaled) f[i] = __fmul_rn(f[i], s);
+  }
+  return make_uint2(pack_bf16x2_rn(f[0], f[1]), pack_bf16x2_rn(f[2], f[3]));
+}
+
 struct Smem {
   uint8_t* stage0;     // stage s starts at stage0 + s * kStageBytes
   uint64_t* full;      // [kStages] TMA + cp.async landed
@@ -165,12 +202,15 @@ struct Smem {
   uint32_t* tmem_base;
 };
 
-template <bool kF16Scale, typename OutT>
-__global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_constant__ CUtensorMap x_map,
-                                                               const __grid_constant__ CUtensorMap nib_map,
-                                                               const void* __restrict__ wscale,
-                                                               const OutT* __restrict__ bias, OutT* __restrict__ y,
-                                                               int M, int N, int K) {
+template <int F, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constant__ CUtensorMap x_map,
+                                                            const __grid_constant__ CUtensorMap q_map,
+                                                            const void* __restrict__ wscale,
+                                                            const OutT* __restrict__ bias, OutT* __restrict__ y,
+                                                            int M, int N, int K) {
+  using T = Traits<F>;
+  constexpr int kStages = T::kStages;
+  constexpr int kStageBytes = T::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Smem sm;
@@ -194,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1 + 32);
+      mbar_init(&sm.full[s], T::kChannel ? 1 : 1 + 32);
       mbar_init(&sm.wready[s], kDequantWarps);
       mbar_init(&sm.empty[s], 1);
     }
@@ -216,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
     // -------------------------------- producer --------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&x_map);
-      tma_prefetch_desc(&nib_map);
+      tma_prefetch_desc(&q_map);
     }
     uint32_t kit = 0;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -228,40 +268,42 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
         if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
         uint8_t* st = sm.stage0 + s * kStageBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full[s], kXBytes + kNibBytes);
+          mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
           tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
-          tma_load_2d(st + kXBytes + kWBytes, &nib_map, &sm.full[s], ks * (kStageK / 2), n0);
+          tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
         }
-        uint8_t* sc = st + kXBytes + kWBytes + kNibBytes;
-        const int g0 = ks * 2;
-        if (kF16Scale) {
-          // one 4-byte word = the two fp16 scales of a row; smem layout [row]
+        if constexpr (!T::kChannel) {
+          uint8_t* sc = st + kXBytes + kWBytes + T::kQBytes;
+          const int g0 = ks * 2;
+          if constexpr (T::kF16Group) {
+            // one 4-byte word = the two fp16 scales of a row; smem layout [row]
 #pragma unroll
-          for (int j = 0; j < kTileN / 32; ++j) {
-            const int r = lane + 32 * j, n = n0 + r;
-            const bool valid = n < N && g0 < groups;
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-            if (valid) src += ((size_t)n * groups + g0) * 2;
-            cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
-          }
-        } else {
-          // smem layout [group][row] (conflict-free reads)
+            for (int j = 0; j < kTileN / 32; ++j) {
+              const int r = lane + 32 * j, n = n0 + r;
+              const bool valid = n < N && g0 < groups;
+              const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+              if (valid) src += ((size_t)n * groups + g0) * 2;
+              cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
+            }
+          } else {
+            // fp32, smem layout [group][row] (conflict-free reads)
 #pragma unroll
-          for (int j = 0; j < 2 * kTileN / 32; ++j) {
-            const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
-            const bool valid = n < N && (g0 + g) < groups;
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-            if (valid) src += ((size_t)n * groups + g0 + g) * 4;
-            cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
+            for (int j = 0; j < 2 * kTileN / 32; ++j) {
+              const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
+              const bool valid = n < N && (g0 + g) < groups;
+              const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+              if (valid) src += ((size_t)n * groups + g0 + g) * 4;
+              cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
+            }
           }
+          cp_async_mbar_arrive_noinc(&sm.full[s]);
         }
-        cp_async_mbar_arrive_noinc(&sm.full[s]);
       }
     }
   } else if (warp >= kDequantWarp0) {
     // -------------------------------- dequant ---------------------------------
     const int dt = (warp - kDequantWarp0) * 32 + lane;  // 0..255
-    const int g = dt / kTileN;                          // group within the stage
+    const int g = dt / kTileN;                          // 32-wide half of the stage
     const int r = dt % kTileN;                          // weight row within the tile
     uint32_t kit = 0;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -270,29 +312,44 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
         const uint32_t ph = (kit / kStages) & 1;
         if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
         uint8_t* st = sm.stage0 + s * kStageBytes;
-        const uint8_t* nib = st + kXBytes + kWBytes;
-        const uint8_t* sc = nib + kNibBytes;
-        // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
-        const uint4 q = *reinterpret_cast<const uint4*>(nib + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
-        float sf;
-        uint32_t s_hi2 = 0, s_lo2 = 0;
-        if (kF16Scale) {
-          sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
-          const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
-          const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
-          const uint32_t hb = __float_as_uint(hi) >> 16;
-          const uint32_t lb = __float_as_uint(lo) >> 16;  // exact truncation (low bits are zero)
-          s_hi2 = hb | (hb << 16);
-          s_lo2 = lb | (lb << 16);
-        } else {
-          sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
-        }
+        const uint8_t* qt = st + kXBytes + kWBytes;
+        const uint8_t* sc = qt + T::kQBytes;
         uint8_t* wrow = st + kXBytes + r * 128;
         const int c0 = 4 * g, sw = r & 7;
-        *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = dequant_word<kF16Scale>(q.x, sf, s_hi2, s_lo2);
-        *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = dequant_word<kF16Scale>(q.y, sf, s_hi2, s_lo2);
-        *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = dequant_word<kF16Scale>(q.z, sf, s_hi2, s_lo2);
-        *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = dequant_word<kF16Scale>(q.w, sf, s_hi2, s_lo2);
+        if constexpr (!T::kInt8) {
+          // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
+          const uint4 q = *reinterpret_cast<const uint4*>(qt + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
+          float sf;
+          uint32_t s_hi2 = 0, s_lo2 = 0;
+          if constexpr (T::kF16Group) {
+            sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
+            const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
+            const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
+            const uint32_t hb = __float_as_uint(hi) >> 16;
+            const uint32_t lb = __float_as_uint(lo) >> 16;  // exact truncation (low bits are zero)
+            s_hi2 = hb | (hb << 16);
+            s_lo2 = lb | (lb << 16);
+          } else {
+            sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
+          }
+          constexpr bool kF16 = T::kF16Group;
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.x, sf, s_hi2, s_lo2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.y, sf, s_hi2, s_lo2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.z, sf, s_hi2, s_lo2);
+          *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.w, sf, s_hi2, s_lo2);
+        } else {
+          // SWIZZLE_64B int8 tile (64-byte rows): chunk c of row r sits at c ^ ((r >> 1) & 3)
+          const float sf = T::kChannel ? 1.0f : reinterpret_cast<const float*>(sc)[g * kTileN + r];
+          const int xr = (r >> 1) & 3;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint4 q = *reinterpret_cast<const uint4*>(qt + r * 64 + (((2 * g + j) ^ xr) << 4));
+            const uint2 a = dequant_int8_word<!T::kChannel>(q.x, sf), b = dequant_int8_word<!T::kChannel>(q.y, sf);
+            const uint2 cc = dequant_int8_word<!T::kChannel>(q.z, sf), d = dequant_int8_word<!T::kChannel>(q.w, sf);
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j) ^ sw) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j + 1) ^ sw) << 4)) = make_uint4(cc.x, cc.y, d.x, d.y);
+          }
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.wready[s]);
@@ -349,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
       const int n = n0 + warp * 32 + lane;
       const bool n_ok = n < N;
       const float b = (bias != nullptr && n_ok) ? to_f32(bias[n]) : 0.0f;
+      const float cs = (T::kChannel && n_ok) ? __half2float(reinterpret_cast<const __half*>(wscale)[n]) : 1.0f;
       const uint32_t taddr = tmem + acc * kAccCols + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < kAccCols; c += 32) {
@@ -359,7 +417,8 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = mbase + j;
-            if (m < M) y[(size_t)m * N + n] = from_f32<OutT>(__uint_as_float(v[j]) + b);
+            const float a = T::kChannel ? __fmul_rn(__uint_as_float(v[j]), cs) : __uint_as_float(v[j]);
+            if (m < M) y[(size_t)m * N + n] = from_f32<OutT>(a + b);
           }
         }
       }
@@ -382,49 +441,68 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_tc_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 bool w4a16_tc_supported(int M, int N, int K, int scale_dtype) {
   (void)N;
-  if (M <= 64) return false;  // the split-K kernel owns the HBM-bound small-M regime
+  if (M <= 64) return false;  // the small-M kernel owns the HBM-bound regime
   if (K % 32 != 0) return false;
   if (scale_dtype == GFX_SCALE_F16 && K % 64 != 0) return false;
   return true;
 }
 
-template <bool F16S, typename OutT>
-static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& nm, const void* ws, const void* bias, void* y, int M,
+template <int F, typename OutT>
+static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const void* ws, const void* bias, void* y, int M,
                        int N, int K, cudaStream_t st, int sms) {
-  auto kern = tc::w4a16_tc_kernel<F16S, OutT>;
+  using T = tc::Traits<F>;
+  auto kern = tc::wq_tc_kernel<F, OutT>;
   static bool attr_set[64] = {false};
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
     if (e != cudaSuccess)
-      return set_error(GFX_ERR_CUDA, "w4a16_tc: cannot set %d bytes of shared memory: %s", tc::kSmemBytes,
+      return set_error(GFX_ERR_CUDA, "wq_tc: cannot set %d bytes of shared memory: %s", T::kSmemBytes,
                        cudaGetErrorString(e));
     attr_set[dev] = true;
   }
   const int tiles = ((N + tc::kTileN - 1) / tc::kTileN) * ((M + tc::kTileM - 1) / tc::kTileM);
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, tc::kThreads, tc::kSmemBytes, st>>>(xm, nm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
-  return check_launch("w4a16_tc_kernel");
+  kern<<<grid, tc::kThreads, T::kSmemBytes, st>>>(xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
+  return check_launch("wq_tc_kernel");
+}
+
+template <int F>
+static int launch_tc_out(int out_dtype, const CUtensorMap& xm, const CUtensorMap& qm, const void* ws,
+                         const void* bias, void* y, int M, int N, int K, cudaStream_t st, int sms) {
+  if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  return launch_tc_t<F, __nv_bfloat16>(xm, qm, ws, bias, y, M, N, K, st, sms);
+}
+
+static int make_x_map(CUtensorMap* xm, const void* x, int M, int K) {
+  return make_tmap_2d(xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, tc::kStageK,
+                      tc::kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
-  CUtensorMap xm, nm;
-  int rc = make_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
-                        tc::kStageK, tc::kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap xm, qm;
+  int rc = make_x_map(&xm, x, M, K);
   if (rc) return rc;
-  rc = make_tmap_2d(&nm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+  rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                     tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
-  const bool f16 = scale_dtype == GFX_SCALE_F16;
-  if (out_dtype == GFX_DTYPE_F32)
-    return f16 ? launch_tc_t<true, float>(xm, nm, ws, bias, y, M, N, K, stream, sms)
-               : launch_tc_t<false, float>(xm, nm, ws, bias, y, M, N, K, stream, sms);
-  if (out_dtype == GFX_DTYPE_F16)
-    return f16 ? launch_tc_t<true, __half>(xm, nm, ws, bias, y, M, N, K, stream, sms)
-               : launch_tc_t<false, __half>(xm, nm, ws, bias, y, M, N, K, stream, sms);
-  return f16 ? launch_tc_t<true, __nv_bfloat16>(xm, nm, ws, bias, y, M, N, K, stream, sms)
-             : launch_tc_t<false, __nv_bfloat16>(xm, nm, ws, bias, y, M, N, K, stream, sms);
+  if (scale_dtype == GFX_SCALE_F16)
+    return launch_tc_out<tc::kInt4GroupF16>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
+  return launch_tc_out<tc::kInt4GroupF32>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
+}
+
+int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
+  CUtensorMap xm, qm;
+  int rc = make_x_map(&xm, x, M, K);
+  if (rc) return rc;
+  rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, tc::kStageK,
+                    tc::kTileN, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  if (per_channel) return launch_tc_out<tc::kInt8ChanF16>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
+  return launch_tc_out<tc::kInt8GroupF32>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
 }
 
 }  // namespace gfx

@@ -276,6 +276,76 @@ def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, b
     return out
 
 
+def gemm_w8a16(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor, bias: torch.Tensor | None,
+               out_dtype: torch.dtype) -> torch.Tensor:
+    """C[M, N] = x[M, K] @ dequant_int8(B, B_scale)^T (+ bias), fp32 accumulate.
+
+    B int8 [N, K]; B_scale float32 [N, K/32] (the reference's block scales,
+    from quantize_int8) or float16 [N] (one scale per output channel, applied
+    to the fp32 accumulator). Checks follow gemm_int8 (binding.cpp:192-213).
+    """
+    if not (x.is_cuda and B.is_cuda):
+        raise RuntimeError("inputs must be on device")
+    if x.device != B.device:
+        raise RuntimeError("x and B must be on the same device")
+    if B.dtype != torch.int8:
+        raise RuntimeError(f"B must be int8, got {B.dtype}")
+    if x.dim() != 2 or B.dim() != 2 or x.shape[1] != B.shape[1] or x.shape[1] % 32 != 0:
+        raise RuntimeError(f"expected x [M, K], B [N, K], K % 32 == 0; got x {tuple(x.shape)} B {tuple(B.shape)}")
+    M, K = x.shape
+    N = B.shape[0]
+    if B_scale.dtype == torch.float16 and B_scale.numel() == N:
+        per_channel = 1
+    elif B_scale.dtype == torch.float32 and B_scale.numel() == N * (K // 32):
+        per_channel = 0
+    else:
+        raise RuntimeError(f"scales must be float32 [N, K/32] = {N * (K // 32)} or float16 [N] = {N} elements, got "
+                           f"{B_scale.dtype} {tuple(B_scale.shape)}")
+    out = torch.empty(M, N, dtype=out_dtype, device=x.device)
+    if M == 0:
+        return out
+    bias_ptr = None
+    if bias is not None:
+        if bias.dtype != out_dtype or bias.numel() != N:
+            raise RuntimeError(f"bias must be {out_dtype} [{N}], got {bias.dtype} {tuple(bias.shape)}")
+        bias = bias.contiguous()
+        bias_ptr = bias.data_ptr()
+    xb = (x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)).contiguous()
+    Bc, Bs = B.contiguous(), B_scale.contiguous()
+    with torch.cuda.device(x.device):
+        _lib.call("w8a16_gemm", xb.data_ptr(), _lib.DTYPE_BF16, Bc.data_ptr(), Bs.data_ptr(), per_channel, bias_ptr,
+                  out.data_ptr(), _dtype_code(out_dtype), M, N, K, 0, None, 0, _stream(x.device))
+    return out
+
+
+def quantize_int8(x: torch.Tensor):
+    """x [M, K] float -> (int8 [M, K], scale float32 [M, K/32]): block-32,
+    scale = amax * (1/127), round-half-even, clamp +-127 (binding.cpp:174-186,
+    int8_gemm.hip:217-246)."""
+    _require_cuda(x, "x")
+    if x.dim() != 2 or x.shape[1] % 32 != 0:
+        raise RuntimeError(f"x must be [M, K] with K % 32 == 0, got {tuple(x.shape)}")
+    xc = x.contiguous()
+    M, K = xc.shape
+    q = torch.empty(M, K, dtype=torch.int8, device=x.device)
+    s = torch.empty(M, K // 32, dtype=torch.float32, device=x.device)
+    if M:
+        with torch.cuda.device(x.device):
+            _lib.call("quantize_int8", xc.data_ptr(), _dtype_code(xc.dtype), q.data_ptr(), s.data_ptr(), M, K,
+                      _stream(x.device))
+    return q, s
+
+
+def quantize_int4(x: torch.Tensor):
+    """x [M, K] float (CUDA) -> (packed int8 [M, K/2], scale float32 [M, K/32]):
+    the reference's activation quantizer (binding.cpp:53-68,
+    int4_gemm_scaled.hip:197-220; scale = amax * (1/7))."""
+    _require_cuda(x, "x")
+    if x.dim() != 2 or x.shape[1] % 32 != 0:
+        raise RuntimeError(f"x must be [M, K] with K % 32 == 0, got {tuple(x.shape)}")
+    return quantize_pack_int4(x)
+
+
 def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                 rotation_group: int = 0) -> torch.Tensor:
     """x [..., K] float, packed weights from quantize_pack_int4 (folded through

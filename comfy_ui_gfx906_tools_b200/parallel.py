@@ -1,0 +1,98 @@
+"""Multi-GPU split of one DiT forward: batch split and token-row split.
+
+B200 re-design of the reference's two-GPU split
+(nodes/ComfyUI-Gfx906Int4/row_split.py): one process per GPU over
+``torch.distributed`` (NCCL over NVLink / NVSwitch) instead of a worker thread
+and PCIe copies, for any world size that divides the work.
+
+  * Batch split (row_split.py:179-189): rank r runs samples
+    [r*B/G, (r+1)*B/G) of the batch through its own replica of the model; no
+    exchange until the optional all-gather of the outputs.
+  * Token-row split (row_split.py:191-206): the image tokens of one sample are
+    split into G contiguous blocks of latent rows; every rank keeps all text
+    tokens. Each block's attention gathers the image keys and values of all
+    ranks with one ``all_gather_into_tensor`` per tensor (the reference swaps
+    K/V with its peer, row_split.py:47-64,87-96); queries stay local, so the
+    int4 linears only ever see the rank's own tokens. Text keys come from the
+    rank's own (replicated) text stream, so they count once (the reference
+    drops rank 1's copy, row_split.py:90-94). RoPE uses each token's true row
+    id, as the reference's post_input offset does (row_split.py:81-85).
+
+A rank that fails raises; its peers' next collective ends with the process
+group's timeout error instead of waiting forever (the reference aborts its
+thread barrier, row_split.py:220-240).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .flux_dit import AttentionExchange
+
+
+class TokenShard(AttentionExchange):
+    """Gathers the image keys/values of every rank (rank order = token order)."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        # t [B, H, L_local, D] -> [B, H, L_local * world, D], rank-major along L
+        t = t.contiguous()
+        B, H, L, D = t.shape
+        out = torch.empty(self.world * B, H, L, D, dtype=t.dtype, device=t.device)  # dim-0 concatenation
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        return out.view(self.world, B, H, L, D).permute(1, 2, 0, 3, 4).reshape(B, H, self.world * L, D)
+
+    def joint_kv(self, txt_k, txt_v, img_k, img_v):
+        return torch.cat([txt_k, self._gather(img_k)], dim=2), torch.cat([txt_v, self._gather(img_v)], dim=2)
+
+
+def row_block(h_tokens: int, rank: int, world: int):
+    """Latent token rows [start, stop) owned by `rank` (contiguous, equal-sized)."""
+    if h_tokens % world != 0:
+        raise ValueError(f"token rows ({h_tokens}) must divide evenly over {world} ranks for the row split")
+    per = h_tokens // world
+    return rank * per, (rank + 1) * per
+
+
+def split_forward_rows(model, img, img_ids, txt, txt_ids, timesteps, y, h_tokens: int, w_tokens: int,
+                       group=None, gather_output: bool = True):
+    """Token-row split forward of one batch on every rank of `group`; returns
+    the full [B, L_img, C] output on every rank (or the local rows)."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    r0, r1 = row_block(h_tokens, rank, world)
+    sl = slice(r0 * w_tokens, r1 * w_tokens)
+    saved = model.exchange
+    model.exchange = TokenShard(group)
+    try:
+        out = model(img[:, sl].contiguous(), img_ids[:, sl].contiguous(), txt, txt_ids, timesteps, y)
+    finally:
+        model.exchange = saved
+    if not gather_output:
+        return out
+    full = torch.empty(world * out.shape[0], *out.shape[1:], dtype=out.dtype, device=out.device)
+    dist.all_gather_into_tensor(full, out.contiguous(), group=group)
+    full = full.view(world, *out.shape)
+    return full.permute(1, 0, 2, 3).reshape(out.shape[0], world * out.shape[1], out.shape[2])
+
+
+def batch_slice(batch: int, rank: int, world: int):
+    if batch % world != 0:
+        raise ValueError(f"batch ({batch}) must divide evenly over {world} ranks for the batch split")
+    per = batch // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+def split_forward_batch(model, img, img_ids, txt, txt_ids, timesteps, y, group=None, gather_output: bool = True):
+    """Batch split forward: each rank runs its slice of the batch; returns the
+    full output on every rank (or the local slice)."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    sl = batch_slice(img.shape[0], rank, world)
+    out = model(img[sl], img_ids[sl], txt[sl], txt_ids[sl], timesteps[sl], y[sl])
+    if not gather_output:
+        return out
+    full = torch.empty(world * out.shape[0], *out.shape[1:], dtype=out.dtype, device=out.device)
+    dist.all_gather_into_tensor(full, out.contiguous(), group=group)
+    return full

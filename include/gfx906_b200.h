@@ -90,11 +90,13 @@ int w4a16_auto_splits(int M, int N, int K);
 /*
  * W8A16 GEMM:  y = x @ dequant_int8(w_q8, w_scale)^T (+ bias)
  * The int8 sibling of w4a16_gemm (gemm_int8, binding.cpp:190-217; weights
- * from quantize_int8, binding.cpp:174-186).
- *   w_q8     int8 [N, K]
+ * from quantize_int8, binding.cpp:174-186), on the tcgen05 kernel for every M.
+ *   w_q8     int8 [N, K];  K % 32 == 0
  *   w_scale  float32 [N, K/32] (block scales, the reference layout) when
- *            scale_per_channel == 0; float16 [N] per-output-channel scale
- *            when scale_per_channel == 1.
+ *            scale_per_channel == 0: each weight becomes bf16(q * scale);
+ *            float16 [N] per-output-channel scale when scale_per_channel == 1:
+ *            the exact codes are multiplied and the fp32 result is scaled.
+ *   workspace is not used (pass NULL, 0).
  */
 int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,
                const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,

@@ -243,3 +243,45 @@ def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
     gotsum = y.double().sum(dim=1).cpu().numpy()
     scale = np.abs(x.float().numpy()).astype(np.float64) @ np.abs(wsum)
     assert np.max(np.abs(gotsum - want) / (scale + 1e-30)) < 2e-3
+
+
+# ---------------------------------------------------------------------------
+# int8 weights (W8A16): BASELINE config 3 layout (per-channel fp16 scale) and
+# the reference's block-32 layout (quantize_int8 output)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("M", [1, 77, 300, 1000])
+@pytest.mark.parametrize("N,K", [(96, 864), (3, 96), (384, 3456)])
+def test_gemm_int8_block_scales(cuda, M, N, K):
+    # bench_int8.py:37-48 shapes: ragged M / N, bias; B from quantize_int8 (block-32 fp32 scales)
+    g = torch.Generator().manual_seed(M + N)
+    w = torch.randn(N, K, generator=g).to(cuda)
+    bq, bs = ops.quantize_int8(w)
+    qw, sw = O.quantize_int8(w.cpu().numpy())
+    assert np.array_equal(bq.cpu().numpy(), qw) and np.array_equal(bs.cpu().numpy(), sw)
+    x = synthetic.activations(M, K, seed=M)
+    bias = torch.randn(N, generator=g)
+    y = ops.gemm_w8a16(x.to(cuda), bq, bs, bias.to(cuda), torch.float32).cpu().numpy()
+    ref = O.w8a16_matmul(x.float().numpy(), qw, sw, bias.numpy())
+    _check(y, ref)
+
+
+@pytest.mark.parametrize("M", [64, 4608])
+def test_gemm_int8_channel_scales_flux(cuda, M):
+    # int8 ~round(N(0,40)) clipped, one fp16 scale per output channel
+    K, N = 3072, 3072
+    q, s = synthetic.int8_weight(N, K, seed=5)
+    x = synthetic.activations(M, K, seed=6)
+    y = ops.gemm_w8a16(x.to(cuda), q.to(cuda), s.to(cuda), None, torch.bfloat16).float()
+    s_blk = np.repeat(s.float().numpy()[:, None], K // 32, axis=1)
+    rows = np.arange(M) if M <= 64 else np.random.default_rng(1).choice(M, 64, replace=False)
+    ref = O.w8a16_matmul(x[rows].float().numpy(), q.numpy(), s_blk)
+    _check(y[torch.from_numpy(rows).to(cuda)].cpu().numpy(), ref)
+    y32 = ops.gemm_w8a16(x.to(cuda), q.to(cuda), s.to(cuda), None, torch.float32)
+    _check(y32[torch.from_numpy(rows).to(cuda)].cpu().numpy(), ref, 1e-5, 1e-5)  # exact codes, fp32 scale
+
+
+def test_quantize_int4_activation_semantics(cuda):
+    x = (torch.randn(64, 256, generator=torch.Generator().manual_seed(9))).to(cuda, torch.float16)
+    p, s = ops.quantize_int4(x)
+    pw, sw = O.quantize_pack_int4(x.float().cpu().numpy(), div_mode="recip")
+    assert np.array_equal(p.cpu().numpy(), pw) and np.array_equal(s.cpu().numpy(), sw)

@@ -1,0 +1,102 @@
+"""Multi-process split logic on the CPU (gloo, world size 2): the token-row and
+batch splits reproduce the single-process forward of the same DiT, and a rank
+that fails makes its peer's collective end with an error (bounded timeout)
+instead of waiting forever (reference: row_split.py:208-241)."""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+H_TOK, W_TOK, TXT, BATCH = 4, 6, 5, 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model_and_inputs():
+    from comfy_ui_gfx906_tools_b200 import flux_dit
+    torch.manual_seed(0)
+    cfg = flux_dit.tiny_config(depth_double=2, depth_single=2)
+    model = flux_dit.FluxDiT(cfg, flux_dit.float_linear_factory("cpu", torch.float32, seed=3), "cpu", torch.float32)
+    with torch.no_grad():
+        for m in model.modules():
+            if isinstance(m, flux_dit.RMSNorm):
+                m.scale.uniform_(0.5, 1.5)
+    inputs = flux_dit.make_inputs(cfg, BATCH, H_TOK, W_TOK, TXT, "cpu", torch.float32, seed=4)
+    return model, inputs
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        import torch.distributed as dist
+        from comfy_ui_gfx906_tools_b200 import parallel
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+        torch.set_num_threads(2)
+        model, inputs = _model_and_inputs()
+        with torch.no_grad():
+            if mode == "fail":
+                if rank == 1:
+                    raise RuntimeError("rank 1 failed before the exchange")
+                try:
+                    parallel.split_forward_rows(model, *inputs, H_TOK, W_TOK)
+                    q.put((rank, "no-error", None))
+                except Exception as e:  # the peer's collective must end with an error
+                    q.put((rank, "error", type(e).__name__))
+                return
+            ref = model(*inputs)
+            if mode == "rows":
+                got = parallel.split_forward_rows(model, *inputs, H_TOK, W_TOK)
+            else:
+                got = parallel.split_forward_batch(model, *inputs)
+        q.put((rank, "ok", float((got - ref).abs().max() / ref.abs().max())))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "exception", traceback.format_exc()))
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(2):
+        results.append(q.get(timeout=120))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return sorted(results)
+
+
+@pytest.mark.parametrize("mode", ["rows", "batch"])
+def test_split_matches_single_process(mode):
+    res = _run(mode)
+    for rank, status, val in res:
+        assert status == "ok", val
+        assert val < 1e-5, (rank, val)
+
+
+def test_failed_rank_surfaces_as_error():
+    res = dict((r, (s, v)) for r, s, v in _run("fail"))
+    assert res[1][0] == "exception" and "rank 1 failed" in res[1][1]
+    assert res[0][0] == "error", res[0]
+
+
+def test_row_block_partition():
+    from comfy_ui_gfx906_tools_b200 import parallel
+    assert [parallel.row_block(128, r, 4) for r in range(4)] == [(0, 32), (32, 64), (64, 96), (96, 128)]
+    with pytest.raises(ValueError):
+        parallel.row_block(10, 0, 4)
+    assert parallel.batch_slice(8, 3, 4) == slice(6, 8)
