@@ -11,7 +11,8 @@ import os
 import threading
 
 _PKG_DIR = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG_DIR, "lib", "libgfx906_b200.so")
+# GFX906_B200_LIB selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("GFX906_B200_LIB") or os.path.join(_PKG_DIR, "lib", "libgfx906_b200.so")
 
 GFX_OK = 0
 GFX_ERR_INVALID = 1

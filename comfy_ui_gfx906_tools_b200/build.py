@@ -61,9 +61,9 @@ def needs_build() -> bool:
     return _newest(_sources() + _headers() + [os.path.abspath(__file__)]) > os.path.getmtime(LIB_PATH)
 
 
-def _compile(src: str, verbose: bool, extra=()) -> str:
-    os.makedirs(OBJ_DIR, exist_ok=True)
-    obj = os.path.join(OBJ_DIR, os.path.basename(src).replace(".cu", ".o"))
+def _compile(src: str, verbose: bool, extra=(), obj_dir: str = OBJ_DIR) -> str:
+    os.makedirs(obj_dir, exist_ok=True)
+    obj = os.path.join(obj_dir, os.path.basename(src).replace(".cu", ".o"))
     cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
     if verbose:
         cmd += ["-Xptxas", "-v"]
@@ -75,28 +75,34 @@ def _compile(src: str, verbose: bool, extra=()) -> str:
     return obj
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, defines=(), out_path: str | None = None) -> str:
+    """Compile and link the library; `defines` (e.g. ["-DNAME=1"]) and
+    `out_path` build a variant elsewhere (the in-tree default is untouched)."""
+    target = out_path or LIB_PATH
+    if not force and not defines and out_path is None and not needs_build():
         return LIB_PATH
-    os.makedirs(LIB_DIR, exist_ok=True)
+    os.makedirs(os.path.dirname(target), exist_ok=True)
     srcs = _sources()
+    obj_dir = OBJ_DIR if not defines else os.path.join(OBJ_DIR, "variant_" + str(abs(hash(tuple(defines)))))
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
-    tmp = LIB_PATH + ".tmp"
+        objs = list(ex.map(lambda s: _compile(s, verbose, tuple(defines), obj_dir), srcs))
+    tmp = target + ".tmp"
     cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lrt", "-lpthread", "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, target)
+    return target
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas register / spill / smem usage")
+    ap.add_argument("-D", dest="defines", action="append", default=[], help="extra preprocessor define (variant build)")
+    ap.add_argument("--out", default=None, help="output path for a variant build")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, defines=["-D" + d for d in a.defines], out_path=a.out))
 
 
 if __name__ == "__main__":

@@ -62,13 +62,24 @@ constexpr int kStageBytesPerRow = kStageK / 2;  // 128 nibble bytes = one SW128 
 constexpr int kGroupsPerStage = kStageK / 32;
 constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 consumer threads
 
+// Build-time tuning (defaults are the shipped configuration).
+#ifndef GFX_SMALLM_MT_NT1
+#define GFX_SMALLM_MT_NT1 4   // m16 tiles per warp when M <= 8
+#endif
+#ifndef GFX_SMALLM_CTAS_PER_SM
+#define GFX_SMALLM_CTAS_PER_SM 2  // resident CTAs per SM for M <= 16
+#endif
+#ifndef GFX_SMALLM_STAGES_F16
+#define GFX_SMALLM_STAGES_F16 4   // smem ring depth, fp16 scales, M <= 16
+#endif
+
 // Warp tiling: kMT m16 tiles per warp (rows), the 8 consumer warps split into
 // kRowSlices row slices x kKParts K parts (each K part owns kGPW of the 8
 // groups of a unit). More m16 tiles per warp amortise the activation
 // fragments; fewer keep the accumulators of larger token tiles in registers.
 template <int NT, int STAGES, bool kF16Scale>
 struct Layout {
-  static constexpr int kMT = NT == 1 ? 4 : 2;
+  static constexpr int kMT = NT == 1 ? GFX_SMALLM_MT_NT1 : 2;
   static constexpr int kRowSlices = kRows / (16 * kMT);
   static constexpr int kKParts = kConsumerWarps / kRowSlices;
   static constexpr int kGPW = kGroupsPerStage / kKParts;  // groups per warp per unit (even)
@@ -119,7 +130,7 @@ __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
 }
 
 template <int NT, int STAGES, bool kF16Scale, typename OutT>
-__global__ void __launch_bounds__(kThreads, NT <= 2 ? 2 : 1) w4a16_smallm_kernel(
+__global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1) w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
     const OutT* __restrict__ bias, OutT* __restrict__ y, float* __restrict__ partials, int* __restrict__ counters,
@@ -442,7 +453,7 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
   p.RB = (N + smallm::kRows - 1) / smallm::kRows;
   p.KS = (K + smallm::kStageK - 1) / smallm::kStageK;
   // resident CTAs per SM follow the stage ring + reduction buffer size
-  p.ctas_per_sm = p.nt == 4 ? 1 : 2;
+  p.ctas_per_sm = p.nt == 4 ? 1 : GFX_SMALLM_CTAS_PER_SM;
   p.stages = p.nt == 4 ? 6 : ((!f16 && p.nt == 2) ? 3 : 4);
   const long long U = (long long)p.RB * p.KS;
   long long G;
@@ -564,8 +575,8 @@ int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale
   a.K = K;
   // stage counts: two resident CTAs per SM for NT <= 2 (<= ~110 KB each), one for NT = 4
   if (f16) {
-    if (p.nt == 1) return launch_smallm_out<1, 4, true>(out_dtype, p, a, stream);
-    if (p.nt == 2) return launch_smallm_out<2, 4, true>(out_dtype, p, a, stream);
+    if (p.nt == 1) return launch_smallm_out<1, GFX_SMALLM_STAGES_F16, true>(out_dtype, p, a, stream);
+    if (p.nt == 2) return launch_smallm_out<2, GFX_SMALLM_STAGES_F16, true>(out_dtype, p, a, stream);
     return launch_smallm_out<4, 6, true>(out_dtype, p, a, stream);
   }
   if (p.nt == 1) return launch_smallm_out<1, 4, false>(out_dtype, p, a, stream);
