@@ -36,6 +36,8 @@ SIGNATURES = {
     "gfx_device_status": (_c_int, [_c_int]),
     "w4a16_gemm": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
                             _c_int, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p]),
+    "w4a16_gemm_noalloc": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,
+                                    _c_int, _c_int, _c_int, _c_int, _c_void_p]),
     "w4a16_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "w4a16_auto_splits": (_c_int, [_c_int, _c_int, _c_int]),
     "w8a16_gemm": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,

@@ -80,6 +80,25 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
                const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
                size_t workspace_bytes, gfx_stream_t stream);
 
+/*
+ * W4A16 GEMM that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory -- a plugin host that passes
+ * only its input/output device pointers and owns the memory budget, or code
+ * that must not issue a synchronising cudaMalloc -- yet need the small-M path,
+ * whose w4a16_gemm call requires a caller-provided scratch workspace.
+ * Same arguments and result as w4a16_gemm without the workspace; M <= 64 only
+ * (M > 64: call w4a16_gemm with a NULL workspace, that kernel needs no
+ * scratch). The scratch is a fixed 8 MiB array in the library's device memory,
+ * held by every GPU that loads the library until the process exits; shapes
+ * needing more are rejected with GFX_ERR_UNSUPPORTED. The first call on a
+ * device looks the array up and clears it (make it before any stream capture).
+ * All calls share the array: calls that overlap on the GPU race, so serialise
+ * them.
+ */
+int w4a16_gemm_noalloc(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+                       const void* bias, void* y, int out_dtype, int M, int N, int K, int splits,
+                       gfx_stream_t stream);
+
 /* Scratch bytes w4a16_gemm needs for (M, N, K, splits) on the current device. */
 size_t w4a16_workspace_bytes(int M, int N, int K, int splits);
 
