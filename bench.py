@@ -1,6 +1,6 @@
 """Benchmark of the int4 W4A16 linear path on B200 (driver contract: one JSON line).
 
-Workload ("flux_linear_sweep"): one step = the six Flux DiT
+Workload (config 2, "flux_linear_sweep"): one step = the six Flux DiT
 linear shapes at hidden 3072 ((K, N) in qkv 3072x9216, proj 3072x3072, mlp-up
 3072x12288, mlp-down 12288x3072, single-fused 3072x21504, single-out
 15360x3072), M = 4608 tokens each, bf16 activations, int4 group-32 weights
@@ -296,7 +296,7 @@ def run_ours(args, world, rank, local):
             del g
         del copies
 
-    # --- int8 weights: the six shapes at M=4608, per-channel fp16 scales ---
+    # --- int8 weights (config 3): the six shapes at M=4608, per-channel fp16 scales ---
     int8 = None
     if not args.no_int8:
         w8 = []
@@ -364,7 +364,7 @@ def run_ours(args, world, rank, local):
 
 
 def run_dit(args, world, rank, local):
-    """the full Flux-architecture DiT forward (random int4
+    """Configs 4-5: the full Flux-architecture DiT forward (random int4
     weights), batch split or token-row split across the ranks."""
     from comfy_ui_gfx906_tools_b200 import flux_dit, ops, parallel
     dev = torch.device("cuda", local)

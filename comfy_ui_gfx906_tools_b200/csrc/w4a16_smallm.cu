@@ -100,9 +100,11 @@ __device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
+// A register-only operation: not volatile, so the compiler may interleave the
+// MMA chains of different tiles with each other and with the loads.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%10, %11, %12, %13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -238,56 +240,69 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
       const int grp = kq * kGPW + gi;
       const int h = grp & 1;  // which 32-group of x box grp/2
       const uint8_t* xs = sc + L::kScaleBytes + (grp >> 1) * L::kXBoxBytes;
-      // B fragments (activations) of this group for each token tile, and the
-      // offset correction p0 = -136 * sum_k x (constant A operand).
-      uint32_t b[NT][4];
-      float p0[NT][4];
+      // All shared-memory loads of this group first (volatile ldmatrix keeps
+      // source order, so loads written after an MMA could not start earlier):
+      // the activation fragments, one nibble word per row and m16 tile, and
+      // the two scales per m16 tile.
+      uint4 xv[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int row = nt * 8 + xrow_in_tile;
         const int chunk = h * 4 + t_;
-        const uint4 v = *reinterpret_cast<const uint4*>(xs + row * 128 + ((chunk ^ (row & 7)) << 4));
-        b[nt][0] = prmt(v.x, v.z, 0x5410);  // step 0, slots (2t, 2t+1)
-        b[nt][1] = prmt(v.x, v.z, 0x7632);  // step 0, slots (2t+8, 2t+9)
-        b[nt][2] = prmt(v.y, v.w, 0x5410);  // step 1
-        b[nt][3] = prmt(v.y, v.w, 0x7632);
+        xv[nt] = *reinterpret_cast<const uint4*>(xs + row * 128 + ((chunk ^ (row & 7)) << 4));
+      }
+      uint32_t wr[kMT], wr8[kMT];
+#pragma unroll
+      for (int mt = 0; mt < kMT; ++mt) {
+        // word t of group grp for rows rbase+g (matrix 0) and rbase+8+g (matrix 1)
+        const int lrow = rs * 16 * kMT + mt * 16 + lm_j + lm_hi * 8;
+        ldmatrix_x2(nib_base + lrow * kStageBytesPerRow + ((grp ^ (lrow & 7)) << 4), wr[mt], wr8[mt]);
+      }
+      float s_r[kMT], s_r8[kMT];
+#pragma unroll
+      for (int mt = 0; mt < kMT; ++mt) {
+        const int r_lo = rs * 16 * kMT + mt * 16 + g_, r_hi = r_lo + 8;
+        if (kF16Scale) {
+          const __half* sch = reinterpret_cast<const __half*>(sc);
+          s_r[mt] = __half2float(sch[r_lo * kGroupsPerStage + grp]);
+          s_r8[mt] = __half2float(sch[r_hi * kGroupsPerStage + grp]);
+        } else {
+          const float* scf = reinterpret_cast<const float*>(sc);
+          s_r[mt] = scf[r_lo * kGroupsPerStage + grp];
+          s_r8[mt] = scf[r_hi * kGroupsPerStage + grp];
+        }
+      }
+      // B fragments and the offset correction p0 = -136 * sum_k x (constant A operand).
+      uint32_t b[NT][4];
+      float p0[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        b[nt][0] = prmt(xv[nt].x, xv[nt].z, 0x5410);  // step 0, slots (2t, 2t+1)
+        b[nt][1] = prmt(xv[nt].x, xv[nt].z, 0x7632);  // step 0, slots (2t+8, 2t+9)
+        b[nt][2] = prmt(xv[nt].y, xv[nt].w, 0x5410);  // step 1
+        b[nt][3] = prmt(xv[nt].y, xv[nt].w, 0x7632);
         const float zero[4] = {0.f, 0.f, 0.f, 0.f};
         mma_bf16_16816(p0[nt], kMinus136x2, kMinus136x2, kMinus136x2, kMinus136x2, b[nt][0], b[nt][1], zero);
         mma_bf16_16816(p0[nt], kMinus136x2, kMinus136x2, kMinus136x2, kMinus136x2, b[nt][2], b[nt][3], p0[nt]);
       }
 #pragma unroll
       for (int mt = 0; mt < kMT; ++mt) {
-        const int rbase = rs * 16 * kMT + mt * 16;
-        // word t of group grp for rows rbase+g (matrix 0) and rbase+8+g (matrix 1)
-        const int lrow = rbase + lm_j + lm_hi * 8;
-        uint32_t wr, wr8;
-        ldmatrix_x2(nib_base + lrow * kStageBytesPerRow + ((grp ^ (lrow & 7)) << 4), wr, wr8);
-        const int r_lo = rbase + g_, r_hi = r_lo + 8;
-        float s_r, s_r8;
-        if (kF16Scale) {
-          const __half* sch = reinterpret_cast<const __half*>(sc);
-          s_r = __half2float(sch[r_lo * kGroupsPerStage + grp]);
-          s_r8 = __half2float(sch[r_hi * kGroupsPerStage + grp]);
-        } else {
-          const float* scf = reinterpret_cast<const float*>(sc);
-          s_r = scf[r_lo * kGroupsPerStage + grp];
-          s_r8 = scf[r_hi * kGroupsPerStage + grp];
-        }
         // step 0: slots (2t,2t+1) <- (n0,n4), (2t+8,2t+9) <- (n1,n5)
         // step 1: slots (2t,2t+1) <- (n2,n6), (2t+8,2t+9) <- (n3,n7)
-        const uint32_t a00 = nib_pair_magic(wr), a01 = nib_pair_magic(wr8);
-        const uint32_t a02 = nib_pair_magic(wr >> 4), a03 = nib_pair_magic(wr8 >> 4);
-        const uint32_t a10 = nib_pair_magic(wr >> 8), a11 = nib_pair_magic(wr8 >> 8);
-        const uint32_t a12 = nib_pair_magic(wr >> 12), a13 = nib_pair_magic(wr8 >> 12);
+        const uint32_t w0 = wr[mt], w1 = wr8[mt];
+        const uint32_t a00 = nib_pair_magic(w0), a01 = nib_pair_magic(w1);
+        const uint32_t a02 = nib_pair_magic(w0 >> 4), a03 = nib_pair_magic(w1 >> 4);
+        const uint32_t a10 = nib_pair_magic(w0 >> 8), a11 = nib_pair_magic(w1 >> 8);
+        const uint32_t a12 = nib_pair_magic(w0 >> 12), a13 = nib_pair_magic(w1 >> 12);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           float p[4];
           mma_bf16_16816(p, a00, a01, a02, a03, b[nt][0], b[nt][1], p0[nt]);
           mma_bf16_16816(p, a10, a11, a12, a13, b[nt][2], b[nt][3], p);
-          acc[mt][nt][0] = fmaf(p[0], s_r, acc[mt][nt][0]);
-          acc[mt][nt][1] = fmaf(p[1], s_r, acc[mt][nt][1]);
-          acc[mt][nt][2] = fmaf(p[2], s_r8, acc[mt][nt][2]);
-          acc[mt][nt][3] = fmaf(p[3], s_r8, acc[mt][nt][3]);
+          acc[mt][nt][0] = fmaf(p[0], s_r[mt], acc[mt][nt][0]);
+          acc[mt][nt][1] = fmaf(p[1], s_r[mt], acc[mt][nt][1]);
+          acc[mt][nt][2] = fmaf(p[2], s_r8[mt], acc[mt][nt][2]);
+          acc[mt][nt][3] = fmaf(p[3], s_r8[mt], acc[mt][nt][3]);
         }
       }
     }

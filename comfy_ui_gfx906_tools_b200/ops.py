@@ -6,8 +6,10 @@ compute routed through this package's C-ABI library (``_lib``):
 
   * ``int4_linear`` (ops.py:167-183) -> ``gemm_w4a16``: bf16 activations
     against the packed int4 weights, fp32 accumulation (weight-only; the
-    reference quantizes activations to int4 as well, see DESIGN notes in the
-    package docstring of ``gemm_int4``);
+    reference's ``gemm_int4`` also quantizes the activations to int4 per
+    32-block, binding.cpp:53-68, which this drop-in does not do: the
+    weight-only product is the one the reference's fp32 dequant-then-matmul
+    oracle defines);
   * ``quantize_pack_int4`` (ops.py:108-126) and ``repack_q4_0_native``
     (ops.py:129-164) run as GPU kernels with results identical to the
     reference's torch code on the tensor's own device (CPU tensors: the

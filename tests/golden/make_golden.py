@@ -74,13 +74,17 @@ def _extract_function(path, func_name, namespace):
     raise KeyError(f"{func_name} not found in {path}")
 
 
+_REPO_ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
 def _bf16_bits(t):
     return t.contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("GFX906_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get(
+        "GFX906_REFERENCE", os.path.join(os.path.dirname(_REPO_ROOT), "reference")))
     args = ap.parse_args()
     ref = args.reference
     node_dir = os.path.join(ref, "nodes", "ComfyUI-Gfx906Int4")

@@ -46,7 +46,7 @@ def test_dit_int4_matches_dequantized_twin(cuda):
 
 
 def test_dit_full_dims_forward_finite(cuda):
-    # BASELINE config 4 dims (19 + 38 blocks, hidden 3072), 1024^2 latent: 64 x 64 patches + 512 text tokens
+    # config-4 dims (19 + 38 blocks, hidden 3072), 1024^2 latent: 64 x 64 patches + 512 text tokens
     cfg = flux_dit.DiTConfig()
     model = flux_dit.FluxDiT(cfg, flux_dit.int4_linear_factory(cuda, seed=3), cuda, torch.bfloat16)
     n_int4 = sum(1 for m in model.modules() if isinstance(m, ops.Gfx906Int4Ops.Linear) and m.quantized)
