@@ -114,10 +114,59 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
 }
 
 // ---------------------------------------------------------------------------
+// thread-block clusters (CTA pairs)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA in the cluster; release/acquire at cluster scope.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on the barrier at the same offset in CTA `rank` of the cluster
+// (default .release.cta semantics: a cluster-scope release would wait for all
+// of the thread's outstanding memory operations, global stores included).
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(mapa_shared(smem_u32(bar), rank)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // TMA (tensor) and Ampere-style cp.async
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel of the
+// stream is still running: pdl_wait() blocks until that kernel has completed
+// and its memory is visible, so every read of data another kernel produced and
+// every global write comes after it. pdl_trigger() lets the next kernel of the
+// stream launch (its CTAs take SMs as this grid's CTAs retire). Both return at
+// once when there is no such dependency.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Prefetch one 2-D box of a tensor map into L2 (no shared memory, no barrier).
+// Safe before pdl_wait(): L2 is the point of coherence, so a line fetched
+// before the previous kernel's writes reach L2 is updated by those writes.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 // 2-D tiled TMA load, completion counted on `bar` in bytes. c0 is the

@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
   }
   __syncthreads();
   if (n_iters <= 0) return;
+  pdl_trigger();
 
   if (warp == kConsumerWarps) {
     // ------------------------------ producer ------------------------------
@@ -174,7 +175,15 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
       tma_prefetch_desc(&nib_map);
       tma_prefetch_desc(&x_map);
       if (scale_tma) tma_prefetch_desc(&scale_map);
+      // the first stages' weight tiles start streaming into L2 while the
+      // previous kernel of the stream finishes
+      const int pre = n_iters < STAGES ? n_iters : STAGES;
+      for (int it = 0; it < pre; ++it) {
+        const long long u = u_begin + it;
+        tma_prefetch_l2_2d(&nib_map, (int)(u % KS) * kStageBytesPerRow, (int)(u / KS) * kRows);
+      }
     }
+    pdl_wait();
     for (int it = 0; it < n_iters; ++it) {
       const int stage = it % STAGES;
       const uint32_t phase = (it / STAGES) & 1;
@@ -212,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
   }
 
   // ------------------------------ consumers -----------------------------
+  pdl_wait();  // outputs, partials and counters are touched only after the previous kernel
   constexpr int kMT = L::kMT, kRowSlices = L::kRowSlices, kKParts = L::kKParts, kGPW = L::kGPW;
   const int rs = warp % kRowSlices;  // row slice: rows rs*16*kMT .. of the row block
   const int kq = warp / kRowSlices;  // K part: groups kq*kGPW .. kq*kGPW + kGPW - 1 of each unit
@@ -530,10 +540,19 @@ static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
                        cudaGetErrorString(e));
     attr_set[dev] = true;
   }
-  dim3 grid(p.G, p.tok_blocks);
-  kern<<<grid, smallm::kThreads, L::kSmemBytes, st>>>(a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
-                                                     (const OutT*)a.bias, (OutT*)a.y, a.part, a.cnt, a.M, a.N, a.K,
-                                                     p.G, p.max_segs);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(p.G, p.tok_blocks);
+  cfg.blockDim = dim3(smallm::kThreads);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
+                                     (const OutT*)a.bias, (OutT*)a.y, a.part, a.cnt, a.M, a.N, a.K, p.G, p.max_segs);
+  if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a16_smallm_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a16_smallm_kernel");
 }
 

@@ -32,6 +32,15 @@
 //               The accumulator is double-buffered (2 x 256 columns = all
 //               512), so the epilogue of tile i overlaps the main loop of
 //               tile i+1.
+// CTA-pair variant (C = 2, opt-in): a cluster of two CTAs on one TPC
+// computes a 256-row x 256-token tile with tcgen05.mma.cta_group::2 (M=256):
+// each CTA dequantizes its own 128 weight rows and TMA-loads HALF of the
+// x tile (128 tokens); the MMA, issued by CTA 0, reads A and B from both
+// CTAs' shared memory and writes each CTA's 128 x 256 accumulator into its own
+// TMEM. Per SM this halves the x bytes per stage (16 KB instead of 32 KB), so
+// six stages fit instead of four. CTA 1's dequant and epilogue warps arrive on
+// CTA 0's barriers (mbarrier.arrive on a shared::cluster address); CTA 0's MMA thread
+// signals both CTAs' barriers with one tcgen05.commit per CTA.
 // Exact int4 dequant: with fp16-valued scales the product code*scale is exact
 // in fp32 and one rounding to bf16 equals the reference's two roundings; it is
 // computed as fma.rn.bf16x2(code, s_hi, code * s_lo) with s = s_hi + s_lo split
@@ -39,6 +48,8 @@
 // General fp32 scales use an fp32 multiply then one cvt.rn to bf16. int8 codes
 // are exact in bf16; a per-channel scale is applied to the fp32 accumulator.
 // Every mbarrier wait is bounded (common.cuh).
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -54,11 +65,17 @@ constexpr int kStageK = 64;       // K per pipeline stage (one 128-byte swizzle 
 constexpr int kUmmaK = 16;
 constexpr int kThreads = 14 * 32;
 constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6, kDequantWarps = 8;
+#ifndef GFX_TC_DEQ_GROUPS
+#define GFX_TC_DEQ_GROUPS 2
+#endif
+// Dequant warp groups working on different stages at once (1, 2, 4 or 8).
+constexpr int kDeqGroups = GFX_TC_DEQ_GROUPS;
+static_assert(kDeqGroups == 1 || kDeqGroups == 2 || kDeqGroups == 4 || kDeqGroups == 8, "bad dequant grouping");
 constexpr int kAccCols = kTileM;  // fp32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
-constexpr int kXBytes = kTileM * kStageK * 2;  // 32 KB
 constexpr int kWBytes = kTileN * kStageK * 2;  // 16 KB
 constexpr int kBarrierBytes = 256;
+constexpr int kSmemLimit = 232448;  // 227 KB per CTA
 
 // Weight formats.
 enum Fmt : int {
@@ -68,8 +85,10 @@ enum Fmt : int {
   kInt8ChanF16 = 3,   // int8, fp16 scale per output channel
 };
 
-template <int F>
+template <int F, int C>
 struct Traits {
+  static constexpr int kXRows = kTileM / C;                    // tokens this CTA loads per stage
+  static constexpr int kXBytes = kXRows * kStageK * 2;         // 32 KB, or 16 KB per CTA of a pair
   static constexpr bool kInt8 = F >= kInt8GroupF32;
   static constexpr bool kChannel = F == kInt8ChanF16;
   static constexpr bool kF16Group = F == kInt4GroupF16;
@@ -77,14 +96,20 @@ struct Traits {
   static constexpr int kQBytes = kTileN * kQRowBytes;
   static constexpr int kScaleBytes = kChannel ? 0 : 1024;            // 128 rows x 2 groups x <= 4 B
   static constexpr int kStageBytes = kXBytes + kWBytes + kQBytes + kScaleBytes;
-  static constexpr int kStages = (1024 + 4 * kStageBytes + kBarrierBytes <= 232448) ? 4 : 3;
+  static constexpr int kFit = (kSmemLimit - 1024 - kBarrierBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
   static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-byte aligned");
+  static_assert(kStages >= 3, "pipeline too shallow");
 };
 
-// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M=128, N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileM >> 3) << 17) |
-                            ((uint32_t)(kTileN >> 4) << 24);
+// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major,
+// M = 128 per CTA (256 for a pair), N = 256.
+template <int C>
+constexpr uint32_t idesc_f16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileM >> 3) << 17) |
+         ((uint32_t)((kTileN * C) >> 4) << 24);
+}
 
 // SMEM matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -92,32 +117,65 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// cta_group::2: one warp of EACH CTA of the pair executes these together.
+template <int C>
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(cols));
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  if constexpr (C == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
 }
 
+template <int C>
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+  if constexpr (C == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+  } else {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+  }
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+template <int C>
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (C == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+// The barrier arrives once every tcgen05.mma this thread issued before has
+// completed. For a pair, one commit per CTA: the barrier at the same offset in
+// CTA `rank` (shared::cluster address).
+template <int C>
+__device__ __forceinline__ void umma_commit(uint64_t* bar, uint32_t rank = 0) {
+  if constexpr (C == 1) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     mapa_shared(smem_u32(bar), rank))
+                 : "memory");
+  }
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -202,15 +260,21 @@ struct Smem {
   uint32_t* tmem_base;
 };
 
-template <int F, typename OutT>
+template <int F, typename OutT, int C>
 __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constant__ CUtensorMap x_map,
                                                             const __grid_constant__ CUtensorMap q_map,
                                                             const void* __restrict__ wscale,
                                                             const OutT* __restrict__ bias, OutT* __restrict__ y,
                                                             int M, int N, int K) {
-  using T = Traits<F>;
+  using T = Traits<F, C>;
   constexpr int kStages = T::kStages;
   constexpr int kStageBytes = T::kStageBytes;
+  constexpr int kXBytes = T::kXBytes;
+  constexpr int kPairRows = kTileN * C;  // weight rows per (pair) tile
+  // Dequant groups must divide the stage count: a group's parity wait on
+  // full[s] is exact only if the load kStages iterations earlier (the same
+  // group's previous item on that stage) has already landed.
+  constexpr int kG = kStages % kDeqGroups == 0 ? kDeqGroups : (kStages % 2 == 0 ? 2 : 1);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Smem sm;
@@ -226,30 +290,38 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_n = (N + kTileN - 1) / kTileN;
+  const uint32_t cr = C == 2 ? cluster_ctarank() : 0u;  // rank within the pair
+  const bool leader = cr == 0;
+  const int tiles_n = (N + kPairRows - 1) / kPairRows;
   const int tiles_m = (M + kTileM - 1) / kTileM;
   const int num_tiles = tiles_n * tiles_m;
+  const int first_tile = blockIdx.x / C, tile_step = gridDim.x / C;
   const int k_stages = (K + kStageK - 1) / kStageK;
   const int groups = K >> 5;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], T::kChannel ? 1 : 1 + 32);
-      mbar_init(&sm.wready[s], kDequantWarps);
+      mbar_init(&sm.wready[s], kDequantWarps / kG * C);  // one group; a pair's arrive on CTA 0
       mbar_init(&sm.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm.acc_full[a], 1);
-      mbar_init(&sm.acc_empty[a], kEpiWarps);
+      mbar_init(&sm.acc_empty[a], kEpiWarps * C);
     }
     mbar_init(sm.drain, 1);
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) tmem_alloc(sm.tmem_base, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc<C>(sm.tmem_base, kTmemCols);
   tc_fence_before();
-  __syncthreads();
+  if constexpr (C == 2) {
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
+  pdl_trigger();
 
   bool ok = true;
   if (warp == kProducerWarp) {
@@ -257,11 +329,19 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     if (lane == 0) {
       tma_prefetch_desc(&x_map);
       tma_prefetch_desc(&q_map);
+      // the first tile's first weight stages stream into L2 while the previous
+      // kernel of the stream finishes
+      if (first_tile < num_tiles) {
+        const int n0 = (first_tile % tiles_n) * kPairRows + (int)cr * kTileN;
+        const int pre = k_stages < kStages ? k_stages : kStages;
+        for (int ks = 0; ks < pre; ++ks) tma_prefetch_l2_2d(&q_map, ks * T::kQRowBytes, n0);
+      }
     }
+    pdl_wait();
     uint32_t kit = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int n0 = (tile % tiles_n) * kTileN;
-      const int m0 = (tile / tiles_n) * kTileM;
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
+      const int m0 = (tile / tiles_n) * kTileM + (int)cr * T::kXRows;
       for (int ks = 0; ks < k_stages; ++ks, ++kit) {
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
@@ -302,102 +382,134 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     }
   } else if (warp >= kDequantWarp0) {
     // -------------------------------- dequant ---------------------------------
+    // reads only shared memory the producer filled after its pdl_wait()
+    // The 8 warps form kG groups; group q dequantizes the stages with
+    // kit % kG == q, so kG stages are in flight at once. A stage holds 256
+    // items (128 rows x two 32-groups); each thread of a group takes kG of
+    // them: items tg, tg + 256/kG, ... (row = item % 128, group = item / 128).
+    constexpr int kGroupThreads = kDequantWarps * 32 / kG;
     const int dt = (warp - kDequantWarp0) * 32 + lane;  // 0..255
-    const int g = dt / kTileN;                          // 32-wide half of the stage
-    const int r = dt % kTileN;                          // weight row within the tile
+    const int q = dt / kGroupThreads, tg = dt % kGroupThreads;
     uint32_t kit = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
       for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        if ((int)(kit % kG) != q) continue;
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
         if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
         uint8_t* st = sm.stage0 + s * kStageBytes;
         const uint8_t* qt = st + kXBytes + kWBytes;
         const uint8_t* sc = qt + T::kQBytes;
-        uint8_t* wrow = st + kXBytes + r * 128;
-        const int c0 = 4 * g, sw = r & 7;
-        if constexpr (!T::kInt8) {
-          // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
-          const uint4 q = *reinterpret_cast<const uint4*>(qt + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
-          float sf;
-          uint32_t s_hi2 = 0, s_lo2 = 0;
-          if constexpr (T::kF16Group) {
-            sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
-            const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
-            const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
-            const uint32_t hb = __float_as_uint(hi) >> 16;
-            const uint32_t lb = __float_as_uint(lo) >> 16;  // exact truncation (low bits are zero)
-            s_hi2 = hb | (hb << 16);
-            s_lo2 = lb | (lb << 16);
-          } else {
-            sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
-          }
-          constexpr bool kF16 = T::kF16Group;
-          *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.x, sf, s_hi2, s_lo2);
-          *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.y, sf, s_hi2, s_lo2);
-          *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.z, sf, s_hi2, s_lo2);
-          *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = dequant_nibble_word<kF16>(q.w, sf, s_hi2, s_lo2);
-        } else {
-          // SWIZZLE_64B int8 tile (64-byte rows): chunk c of row r sits at c ^ ((r >> 1) & 3)
-          const float sf = T::kChannel ? 1.0f : reinterpret_cast<const float*>(sc)[g * kTileN + r];
-          const int xr = (r >> 1) & 3;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint4 q = *reinterpret_cast<const uint4*>(qt + r * 64 + (((2 * g + j) ^ xr) << 4));
-            const uint2 a = dequant_int8_word<!T::kChannel>(q.x, sf), b = dequant_int8_word<!T::kChannel>(q.y, sf);
-            const uint2 cc = dequant_int8_word<!T::kChannel>(q.z, sf), d = dequant_int8_word<!T::kChannel>(q.w, sf);
-            *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j) ^ sw) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
-            *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j + 1) ^ sw) << 4)) = make_uint4(cc.x, cc.y, d.x, d.y);
+        for (int item_j = 0; item_j < kG; ++item_j) {
+          const int item = tg + item_j * kGroupThreads;
+          const int g = item / kTileN;  // 32-wide half of the stage
+          const int r = item % kTileN;  // weight row within the tile
+          uint8_t* wrow = st + kXBytes + r * 128;
+          const int c0 = 4 * g, sw = r & 7;
+          if constexpr (!T::kInt8) {
+            // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
+            const uint4 qw = *reinterpret_cast<const uint4*>(qt + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
+            float sf;
+            uint32_t s_hi2 = 0, s_lo2 = 0;
+            if constexpr (T::kF16Group) {
+              sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
+              const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
+              const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
+              const uint32_t hb = __float_as_uint(hi) >> 16;
+              const uint32_t lb = __float_as_uint(lo) >> 16;  // exact truncation (low bits are zero)
+              s_hi2 = hb | (hb << 16);
+              s_lo2 = lb | (lb << 16);
+            } else {
+              sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
+            }
+            constexpr bool kF16 = T::kF16Group;
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 0) ^ sw) << 4)) = dequant_nibble_word<kF16>(qw.x, sf, s_hi2, s_lo2);
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 1) ^ sw) << 4)) = dequant_nibble_word<kF16>(qw.y, sf, s_hi2, s_lo2);
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 2) ^ sw) << 4)) = dequant_nibble_word<kF16>(qw.z, sf, s_hi2, s_lo2);
+            *reinterpret_cast<uint4*>(wrow + (((c0 + 3) ^ sw) << 4)) = dequant_nibble_word<kF16>(qw.w, sf, s_hi2, s_lo2);
+          } else {
+            // SWIZZLE_64B int8 tile (64-byte rows): chunk c of row r sits at c ^ ((r >> 1) & 3)
+            const float sf = T::kChannel ? 1.0f : reinterpret_cast<const float*>(sc)[g * kTileN + r];
+            const int xr = (r >> 1) & 3;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint4 qw = *reinterpret_cast<const uint4*>(qt + r * 64 + (((2 * g + j) ^ xr) << 4));
+              const uint2 a = dequant_int8_word<!T::kChannel>(qw.x, sf), b = dequant_int8_word<!T::kChannel>(qw.y, sf);
+              const uint2 cc = dequant_int8_word<!T::kChannel>(qw.z, sf), d = dequant_int8_word<!T::kChannel>(qw.w, sf);
+              *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j) ^ sw) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+              *reinterpret_cast<uint4*>(wrow + (((c0 + 2 * j + 1) ^ sw) << 4)) = make_uint4(cc.x, cc.y, d.x, d.y);
+            }
           }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.wready[s]);
+        if (lane == 0) {
+          // this CTA's x slice and dequantized rows of stage s are in place
+          if constexpr (C == 1) {
+            mbar_arrive(&sm.wready[s]);
+          } else {
+            mbar_arrive_cluster(&sm.wready[s], 0);
+          }
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------- MMA -----------------------------------
-    uint32_t kit = 0;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      if (!mbar_wait(&sm.acc_empty[acc], aph ^ 1, kDevErrMmaBarrierTimeout)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t d_tmem = tmem + acc * kAccCols;
-      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
-        const int s = kit % kStages;
-        const uint32_t ph = (kit / kStages) & 1;
-        if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout) ||
-            !mbar_wait(&sm.wready[s], ph, kDevErrFullBarrierTimeout)) {
-          ok = false;
-          break;
-        }
+    // One thread of CTA 0 issues for the pair; CTA 1's MMA warp only waits for
+    // the drain before the collective TMEM release.
+    if (leader) {
+      constexpr uint32_t kId = idesc_f16<C>();
+      uint32_t kit = 0;
+      int it = 0;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&sm.acc_empty[acc], aph ^ 1, kDevErrMmaBarrierTimeout)) { ok = false; break; }
         tc_fence_after();
-        if (lane == 0) {
-          const uint32_t xa = smem_u32(sm.stage0 + s * kStageBytes);
-          const uint32_t wa = xa + kXBytes;
-          const uint64_t adesc = sw128_desc(wa), bdesc = sw128_desc(xa);
-#pragma unroll
-          for (int k = 0; k < kStageK / kUmmaK; ++k) {
-            // advance 16 elements (32 bytes) along K inside the swizzle atom
-            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc, (ks | k) != 0);
+        const uint32_t d_tmem = tmem + acc * kAccCols;
+        for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+          const int s = kit % kStages;
+          const uint32_t ph = (kit / kStages) & 1;
+          // wready[s] complete => every arriving dequant warp saw its CTA's full[s]
+          if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout) ||
+              !mbar_wait(&sm.wready[s], ph, kDevErrFullBarrierTimeout)) {
+            ok = false;
+            break;
           }
-          umma_commit(&sm.empty[s]);
-          if (ks == k_stages - 1) umma_commit(&sm.acc_full[acc]);
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t xa = smem_u32(sm.stage0 + s * kStageBytes);
+            const uint32_t wa = xa + kXBytes;
+            const uint64_t adesc = sw128_desc(wa), bdesc = sw128_desc(xa);
+#pragma unroll
+            for (int k = 0; k < kStageK / kUmmaK; ++k) {
+              // advance 16 elements (32 bytes) along K inside the swizzle atom
+              umma_f16<C>(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kId, (ks | k) != 0);
+            }
+#pragma unroll
+            for (uint32_t rk = 0; rk < (uint32_t)C; ++rk) {
+              umma_commit<C>(&sm.empty[s], rk);
+              if (ks == k_stages - 1) umma_commit<C>(&sm.acc_full[acc], rk);
+            }
+          }
+          __syncwarp();
         }
-        __syncwarp();
       }
+      // drain: every MMA this thread issued has completed before TMEM is freed
+      if (lane == 0) {
+#pragma unroll
+        for (uint32_t rk = 0; rk < (uint32_t)C; ++rk) umma_commit<C>(sm.drain, rk);
+      }
+      __syncwarp();
     }
-    // drain: every MMA this thread issued has completed before TMEM is freed
-    if (lane == 0) umma_commit(sm.drain);
-    __syncwarp();
     mbar_wait(sm.drain, 0, kDevErrMmaBarrierTimeout);
   } else {
     // -------------------------------- epilogue --------------------------------
+    pdl_wait();  // y, bias and channel scales are touched only after the previous kernel
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
-      const int n0 = (tile % tiles_n) * kTileN;
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step, ++it) {
+      const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
       const int m0 = (tile / tiles_n) * kTileM;
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
@@ -424,14 +536,24 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+      if (lane == 0) {
+        if constexpr (C == 1) {
+          mbar_arrive(&sm.acc_empty[acc]);
+        } else {
+          mbar_arrive_cluster(&sm.acc_empty[acc], 0);
+        }
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (C == 2) {
+    cluster_sync_all();  // no CTA leaves while its peer may still touch its barriers or smem
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc<C>(tmem, kTmemCols);
 }
 
 }  // namespace tc
@@ -447,62 +569,111 @@ bool w4a16_tc_supported(int M, int N, int K, int scale_dtype) {
   return true;
 }
 
-template <int F, typename OutT>
+// CTA count per tile. One CTA is the default: on B200 the pair variant
+// (cta_group::2) measured 2-8% slower on the Flux shapes at M = 4608 although
+// it halves the activation bytes per SM, so the per-SM limit is not the x
+// tile traffic. GFX906_B200_TC_CTA=2 selects the pair (tests, measurement).
+static int tc_ctas(int M) {
+  (void)M;
+  const char* e = getenv("GFX906_B200_TC_CTA");
+  if (e && e[0] == '2' && e[1] == 0) return 2;
+  return 1;
+}
+
+template <int F, typename OutT, int C>
 static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const void* ws, const void* bias, void* y, int M,
                        int N, int K, cudaStream_t st, int sms) {
-  using T = tc::Traits<F>;
-  auto kern = tc::wq_tc_kernel<F, OutT>;
+  using T = tc::Traits<F, C>;
+  auto kern = tc::wq_tc_kernel<F, OutT, C>;
   static bool attr_set[64] = {false};
+  static int max_clusters[64] = {0};
   const int dev = current_device();
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  const bool cached = dev >= 0 && dev < 64 && attr_set[dev];
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = T::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 1;
+  if (C == 2) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
+  int clusters = sms / C;
+  if (!cached) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
     if (e != cudaSuccess)
       return set_error(GFX_ERR_CUDA, "wq_tc: cannot set %d bytes of shared memory: %s", T::kSmemBytes,
                        cudaGetErrorString(e));
-    attr_set[dev] = true;
+    if (C == 2) {
+      // pairs must sit on two SMs of one cluster slot; ask how many fit at once
+      cfg.gridDim = dim3(2 * clusters);
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        return set_error(GFX_ERR_CUDA, "wq_tc: no co-resident CTA pair possible: %s", cudaGetErrorString(e));
+      }
+      if (dev >= 0 && dev < 64) max_clusters[dev] = n;
+      clusters = n < clusters ? n : clusters;
+    }
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  } else if (C == 2 && max_clusters[dev] > 0 && max_clusters[dev] < clusters) {
+    clusters = max_clusters[dev];
   }
-  const int tiles = ((N + tc::kTileN - 1) / tc::kTileN) * ((M + tc::kTileM - 1) / tc::kTileM);
-  const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, tc::kThreads, T::kSmemBytes, st>>>(xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
+  const int rows = tc::kTileN * C;
+  const int tiles = ((N + rows - 1) / rows) * ((M + tc::kTileM - 1) / tc::kTileM);
+  const int units = tiles < clusters ? tiles : clusters;
+  cfg.gridDim = dim3(C * units);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
+  if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "wq_tc_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("wq_tc_kernel");
 }
 
 template <int F>
-static int launch_tc_out(int out_dtype, const CUtensorMap& xm, const CUtensorMap& qm, const void* ws,
-                         const void* bias, void* y, int M, int N, int K, cudaStream_t st, int sms) {
-  if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float>(xm, qm, ws, bias, y, M, N, K, st, sms);
-  if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half>(xm, qm, ws, bias, y, M, N, K, st, sms);
-  return launch_tc_t<F, __nv_bfloat16>(xm, qm, ws, bias, y, M, N, K, st, sms);
-}
-
-static int make_x_map(CUtensorMap* xm, const void* x, int M, int K) {
-  return make_tmap_2d(xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, tc::kStageK,
-                      tc::kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
+static int launch_tc_out(int out_dtype, const void* x, const CUtensorMap& qm, const void* ws, const void* bias,
+                         void* y, int M, int N, int K, cudaStream_t st, int sms) {
+  const int C = tc_ctas(M);
+  CUtensorMap xm;
+  // x box: 64 K-elements x (256 tokens, or the 128 of one CTA of a pair), SWIZZLE_128B
+  int rc = make_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+                        tc::kStageK, tc::kTileM / C, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (C == 2) {
+    if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
+    if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
+    return launch_tc_t<F, __nv_bfloat16, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  }
+  if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  return launch_tc_t<F, __nv_bfloat16, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
 }
 
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
-  CUtensorMap xm, qm;
-  int rc = make_x_map(&xm, x, M, K);
-  if (rc) return rc;
-  rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+  CUtensorMap qm;
+  int rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                     tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   if (scale_dtype == GFX_SCALE_F16)
-    return launch_tc_out<tc::kInt4GroupF16>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
-  return launch_tc_out<tc::kInt4GroupF32>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
+    return launch_tc_out<tc::kInt4GroupF16>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
+  return launch_tc_out<tc::kInt4GroupF32>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
 }
 
 int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
-  CUtensorMap xm, qm;
-  int rc = make_x_map(&xm, x, M, K);
-  if (rc) return rc;
-  rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, tc::kStageK,
+  CUtensorMap qm;
+  int rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, tc::kStageK,
                     tc::kTileN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
-  if (per_channel) return launch_tc_out<tc::kInt8ChanF16>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
-  return launch_tc_out<tc::kInt8GroupF32>(out_dtype, xm, qm, ws, bias, y, M, N, K, stream, sms);
+  if (per_channel) return launch_tc_out<tc::kInt8ChanF16>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
+  return launch_tc_out<tc::kInt8GroupF32>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
 }
 
 }  // namespace gfx

@@ -223,9 +223,48 @@ def test_gemm_large_m_deterministic(cuda):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("M,N,K", [(100, 384, 512), (300, 1000, 3072), (777, 129, 64), (1024, 640, 2048)])
+@pytest.mark.parametrize("f16_scales", [False, True])
+def test_gemm_large_m_cta_pair_matches_single_cta(cuda, monkeypatch, M, N, K, f16_scales):
+    """The opt-in CTA-pair kernel (cta_group::2) and the default one-CTA
+    kernel, selected through GFX906_B200_TC_CTA, compute the same products
+    with the same K order; both are checked against the oracle too."""
+    p, s, pd, sd = _weights(N, K, 71 + M, cuda)
+    if f16_scales:
+        sd = ops.scales_to_f16_if_exact(sd)
+    xn, xd = _x(M, K, 72 + M, cuda)
+    out = {}
+    for c in ("1", "2"):
+        monkeypatch.setenv("GFX906_B200_TC_CTA", c)
+        out[c] = ops.gemm_w4a16(xd, pd, sd, None, torch.float32)
+    monkeypatch.delenv("GFX906_B200_TC_CTA")
+    torch.testing.assert_close(out["1"], out["2"], rtol=1e-5, atol=1e-5 * out["1"].abs().max().item())
+    for c in ("1", "2"):
+        _check(out[c].cpu().numpy(), O.w4a16_matmul_bf16w(xn, p, s), 1e-5, 1e-5)
+
+
+@pytest.mark.parametrize("per_channel", [False, True])
+def test_gemm_int8_cta_pair_matches_single_cta(cuda, monkeypatch, per_channel):
+    M, N, K = 640, 384, 1024
+    rng = np.random.default_rng(81)
+    w = np.clip(np.round(rng.normal(0, 40, (N, K))), -127, 127).astype(np.int8)
+    xn, xd = _x(M, K, 82, cuda)
+    if per_channel:
+        sc = (np.abs(rng.normal(0, 0.01, N)) + 1e-4).astype(np.float16)
+    else:
+        sc = (np.abs(rng.normal(0, 0.01, (N, K // 32))) + 1e-4).astype(np.float32)
+    wd, sdd = torch.from_numpy(w).to(cuda), torch.from_numpy(sc).to(cuda)
+    out = {}
+    for c in ("1", "2"):
+        monkeypatch.setenv("GFX906_B200_TC_CTA", c)
+        out[c] = ops.gemm_w8a16(xd, wd, sdd, None, torch.float32)
+    monkeypatch.delenv("GFX906_B200_TC_CTA")
+    torch.testing.assert_close(out["1"], out["2"], rtol=1e-5, atol=1e-5 * out["1"].abs().max().item())
+
+
 @pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
 def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
-    """BASELINE config 2 at full size. The oracle checks 96 sampled token rows
+    """The Flux linear sweep (config 2) at full size. The oracle checks 96 sampled token rows
     exactly (all N outputs each) and every row through a size-independent
     checksum: sum_n Y[m, n] == X[m] . sum_n W[n] (linearity), in fp64."""
     M = 4608
@@ -246,7 +285,7 @@ def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
 
 
 # ---------------------------------------------------------------------------
-# int8 weights (W8A16): BASELINE config 3 layout (per-channel fp16 scale) and
+# int8 weights (W8A16): the config-3 layout (per-channel fp16 scale) and
 # the reference's block-32 layout (quantize_int8 output)
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("M", [1, 77, 300, 1000])
