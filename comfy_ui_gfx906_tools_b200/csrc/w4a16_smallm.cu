@@ -437,8 +437,17 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
           const int tok = i / kRows, r = i % kRows;
           const int n = n0 + r;
           if (n >= N || tok0 + tok >= M) continue;
+          // loads issued eight at a time, added in segment order (deterministic)
           float v = 0.0f;
-          for (int s = 0; s < nsegs; ++s) v += __ldcg(part + (size_t)s * (kTok * kRows) + i);
+          for (int s0 = 0; s0 < nsegs; s0 += 8) {
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              t[j] = s0 + j < nsegs ? __ldcg(part + (size_t)(s0 + j) * (kTok * kRows) + i) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (s0 + j < nsegs) v += t[j];
+          }
           if (bias) v += to_f32(bias[n]);
           y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v);
         }
@@ -486,9 +495,22 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
     const int s = splits_req > p.KS ? p.KS : splits_req;
     G = (long long)p.RB * s;  // classic split-K as a special case of the unit partition
   } else {
-    G = (long long)sms * p.ctas_per_sm / p.tok_blocks;
-    if (G < 1) G = 1;
-    if (G > U) G = U;
+    long long slots = (long long)sms * p.ctas_per_sm / p.tok_blocks;
+    if (slots < 1) slots = 1;
+    // A classic split over a divisor s of KS that fills >= 90% of the resident
+    // slots: every CTA then covers one aligned K segment of one row block (one
+    // segment end per CTA). Otherwise stream-K over all slots for balance.
+    int best_s = 0;
+    for (int s = 1; s <= p.KS; ++s) {
+      if (p.KS % s) continue;
+      if ((long long)p.RB * s > slots) break;
+      best_s = s;
+    }
+    if (best_s > 0 && (long long)p.RB * best_s * 10 >= slots * 9) {
+      G = (long long)p.RB * best_s;
+    } else {
+      G = slots > U ? U : slots;
+    }
   }
   p.G = (int)G;
   // segments per row block: a row block spans KS units and every CTA range
