@@ -419,8 +419,10 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int cc = 0; cc < 2; ++cc)
-                mine[(nt * 8 + tok_perm(2 * t_ + cc)) * kRows + r] = acc[mt][nt][half * 2 + cc];
+              for (int cc = 0; cc < 2; ++cc) {
+                const int tok = nt * 8 + tok_perm(2 * t_ + cc);
+                if (tok0 + tok < M) mine[tok * kRows + r] = acc[mt][nt][half * 2 + cc];  // valid tokens only
+              }
           }
         __threadfence();
       }
@@ -431,25 +433,40 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1
       consumer_sync();
       if (*s_flag) {
         __threadfence();
-        // 3) last arrival: fixed-order sum over the segments, + bias, store, re-arm
+        // 3) last arrival: fixed-order sum over the segments, + bias, store, re-arm.
+        // Items are four consecutive rows of one valid token (float4 loads);
+        // each thread issues a batch of eight segments' loads before adding.
         const int tc = threadIdx.x;  // 0..255 (consumers)
-        for (int i = tc; i < kTok * kRows; i += kConsumerWarps * 32) {
-          const int tok = i / kRows, r = i % kRows;
-          const int n = n0 + r;
-          if (n >= N || tok0 + tok >= M) continue;
-          // loads issued eight at a time, added in segment order (deterministic)
-          float v = 0.0f;
+        const int vt = (M - tok0) < kTok ? (M - tok0) : kTok;  // valid tokens of this token block
+        constexpr int kQuads = kRows / 4;
+        for (int item = tc; item < vt * kQuads; item += kConsumerWarps * 32) {
+          const int tok = item / kQuads, r = (item % kQuads) * 4;
+          const float* src = part + (size_t)tok * kRows + r;
+          float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           for (int s0 = 0; s0 < nsegs; s0 += 8) {
-            float t[8];
+            float4 t[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              t[j] = s0 + j < nsegs ? __ldcg(part + (size_t)(s0 + j) * (kTok * kRows) + i) : 0.0f;
+              t[j] = s0 + j < nsegs ? __ldcg(reinterpret_cast<const float4*>(src + (size_t)(s0 + j) * (kTok * kRows)))
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              if (s0 + j < nsegs) v += t[j];
+              if (s0 + j < nsegs) {
+                v.x += t[j].x;
+                v.y += t[j].y;
+                v.z += t[j].z;
+                v.w += t[j].w;
+              }
           }
-          if (bias) v += to_f32(bias[n]);
-          y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v);
+          const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = n0 + r + e;
+            if (n >= N) continue;
+            float o = vv[e];
+            if (bias) o += to_f32(bias[n]);
+            y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(o);
+          }
         }
         if (tc == 0) *counter = 0;
       }
