@@ -296,6 +296,40 @@ def run_ours(args, world, rank, local):
             del g
         del copies
 
+    # --- M <= 16 on N > 1 GPUs: output-channel split of each GEMM (one all-gather of y) ---
+    tp = None
+    if world > 1 and not args.no_small:
+        import math
+        import torch.distributed as dist
+        from comfy_ui_gfx906_tools_b200 import parallel
+        full_bytes = sum(N * K // 2 + N * (K // 32) * 2 for (_, K, N) in SHAPES)
+        ncopy = max(3, math.ceil(3 * 126e6 * world / full_bytes))  # per-rank shards of all copies > 2x L2
+        shard_sets = []
+        for c in range(ncopy):
+            cp = weights if c == 0 else make_weights(dev, seed=5000 + 100 * c)
+            sh = []
+            for (_, K, N, p, s) in cp:
+                n0, n1 = parallel.channel_block(N, rank, world)
+                sh.append((K, N, p[n0:n1].contiguous(), s[n0:n1].contiguous()))
+            shard_sets.append(sh)
+            del cp
+        tp = {"copies": ncopy, "split": f"output channels / {world}, all_gather_into_tensor of y"}
+        for Ms in (1, 16):
+            xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev) for i, (_, K, _) in enumerate(SHAPES)]
+            outs = [torch.empty(world * Ms, N // world, dtype=torch.bfloat16, device=dev) for (_, _, N) in SHAPES]
+
+            def tp_pass():
+                for sh in shard_sets:
+                    for (K, N, p, s), x, o in zip(sh, xsm, outs):
+                        y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+                        dist.all_gather_into_tensor(o, y)
+            reps = 5
+            ms = max_over_ranks(time_steps(tp_pass, reps, 2, world, dev, stream) / reps, world, dev)
+            nbytes = ncopy * sum(N * K // 2 + N * (K // 32) * 2 + Ms * K * 2 + Ms * N * 2 for (_, K, N) in SHAPES)
+            tp[f"M{Ms}"] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (ncopy * len(SHAPES)),
+                            "frac_hbm_aggregate": (nbytes / (ms * 1e-3) / 1e9) / (world * pk["hbm_gbs"])}
+        del shard_sets
+
     # --- int8 weights (config 3): the six shapes at M=4608, per-channel fp16 scales ---
     int8 = None
     if not args.no_int8:
@@ -358,6 +392,7 @@ def run_ours(args, world, rank, local):
                          "frac": achieved / peak, "peak_kind": f"bf16 dense sustained ({pk['source']})",
                          "frac_of_burst": achieved / pk["bf16_tflops"], "traffic": traffic},
             "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8,
+            **({"small_m_channel_split": tp} if tp is not None else {}),
             "gpu_launches": args.steps * len(weights), "clocks": clocks.summary(),
         }
         print(json.dumps(out))

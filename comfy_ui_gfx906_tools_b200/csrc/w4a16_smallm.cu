@@ -19,7 +19,9 @@
 //    boxes) into a shared-memory ring.
 //  * Eight consumer warps = 2 row slices (64 rows, 4 m16 tiles) x 4 K quarters
 //    (one pair of 32-groups of the unit each), so one activation fragment feeds
-//    64 weight rows. A warp reads one 32-bit nibble word per row and group
+//    64 weight rows (M <= 16; two CTAs per SM for M <= 8, one with 168
+//    registers per thread for 8 < M <= 16; M > 16 uses 4 row slices of 2
+//    tiles x 2 K halves). A warp reads one 32-bit nibble word per row and group
 //    with ldmatrix (conflict-free through the swizzle) and turns each nibble
 //    pair into bf16x2 "magic" values 128 + (code + 8) with one LOP3. The MMA
 //    (mma.sync m16n8k16, weights = 16-row A, tokens = 8-column B) multiplies
@@ -67,10 +69,19 @@ constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 
 #define GFX_SMALLM_MT_NT1 4   // m16 tiles per warp when M <= 8
 #endif
 #ifndef GFX_SMALLM_CTAS_PER_SM
-#define GFX_SMALLM_CTAS_PER_SM 2  // resident CTAs per SM for M <= 16
+#define GFX_SMALLM_CTAS_PER_SM 2  // resident CTAs per SM for M <= 8
 #endif
 #ifndef GFX_SMALLM_STAGES_F16
-#define GFX_SMALLM_STAGES_F16 4   // smem ring depth, fp16 scales, M <= 16
+#define GFX_SMALLM_STAGES_F16 4   // smem ring depth, fp16 scales, M <= 8
+#endif
+#ifndef GFX_SMALLM_MT_NT2
+#define GFX_SMALLM_MT_NT2 4       // m16 tiles per warp when 8 < M <= 16
+#endif
+#ifndef GFX_SMALLM_CTAS_NT2
+#define GFX_SMALLM_CTAS_NT2 1     // resident CTAs per SM when 8 < M <= 16 (168 registers)
+#endif
+#ifndef GFX_SMALLM_STAGES_NT2
+#define GFX_SMALLM_STAGES_NT2 4   // smem ring depth, fp16 scales, 8 < M <= 16
 #endif
 
 // Warp tiling: kMT m16 tiles per warp (rows), the 8 consumer warps split into
@@ -79,7 +90,7 @@ constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 
 // fragments; fewer keep the accumulators of larger token tiles in registers.
 template <int NT, int STAGES, bool kF16Scale>
 struct Layout {
-  static constexpr int kMT = NT == 1 ? GFX_SMALLM_MT_NT1 : 2;
+  static constexpr int kMT = NT == 1 ? GFX_SMALLM_MT_NT1 : (NT == 2 ? GFX_SMALLM_MT_NT2 : 2);
   static constexpr int kRowSlices = kRows / (16 * kMT);
   static constexpr int kKParts = kConsumerWarps / kRowSlices;
   static constexpr int kGPW = kGroupsPerStage / kKParts;  // groups per warp per unit (even)
@@ -132,7 +143,8 @@ __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
 }
 
 template <int NT, int STAGES, bool kF16Scale, typename OutT>
-__global__ void __launch_bounds__(kThreads, NT <= 2 ? GFX_SMALLM_CTAS_PER_SM : 1) w4a16_smallm_kernel(
+__global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (NT == 2 ? GFX_SMALLM_CTAS_NT2 : 1))
+    w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
     const OutT* __restrict__ bias, OutT* __restrict__ y, float* __restrict__ partials, int* __restrict__ counters,
@@ -504,7 +516,7 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
   p.RB = (N + smallm::kRows - 1) / smallm::kRows;
   p.KS = (K + smallm::kStageK - 1) / smallm::kStageK;
   // resident CTAs per SM follow the stage ring + reduction buffer size
-  p.ctas_per_sm = p.nt == 4 ? 1 : GFX_SMALLM_CTAS_PER_SM;
+  p.ctas_per_sm = p.nt == 4 ? 1 : (p.nt == 2 ? GFX_SMALLM_CTAS_NT2 : GFX_SMALLM_CTAS_PER_SM);
   p.stages = p.nt == 4 ? 6 : ((!f16 && p.nt == 2) ? 3 : 4);
   const long long U = (long long)p.RB * p.KS;
   long long G;
@@ -649,7 +661,7 @@ int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale
   // stage counts: two resident CTAs per SM for NT <= 2 (<= ~110 KB each), one for NT = 4
   if (f16) {
     if (p.nt == 1) return launch_smallm_out<1, GFX_SMALLM_STAGES_F16, true>(out_dtype, p, a, stream);
-    if (p.nt == 2) return launch_smallm_out<2, GFX_SMALLM_STAGES_F16, true>(out_dtype, p, a, stream);
+    if (p.nt == 2) return launch_smallm_out<2, GFX_SMALLM_STAGES_NT2, true>(out_dtype, p, a, stream);
     return launch_smallm_out<4, 6, true>(out_dtype, p, a, stream);
   }
   if (p.nt == 1) return launch_smallm_out<1, 4, false>(out_dtype, p, a, stream);

@@ -96,3 +96,60 @@ def split_forward_batch(model, img, img_ids, txt, txt_ids, timesteps, y, group=N
     full = torch.empty(world * out.shape[0], *out.shape[1:], dtype=out.dtype, device=out.device)
     dist.all_gather_into_tensor(full, out.contiguous(), group=group)
     return full
+
+
+def channel_block(n: int, rank: int, world: int):
+    """Output channels [start, stop) owned by `rank` in the output-channel split."""
+    if n % world != 0:
+        raise ValueError(f"output channels ({n}) must divide evenly over {world} ranks for the channel split")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+class ChannelShardLinear(torch.nn.Module):
+    """Output-channel split of one int4 linear for the M <= 16 (HBM-bound) case.
+
+    Rank r keeps rows [r*N/G, (r+1)*N/G) of ``weight_q4`` / ``weight_scale`` /
+    ``bias`` of a ``Gfx906Int4Ops.Linear`` and streams only those, so the
+    ranks together read the weight at G times one GPU's HBM bandwidth; one
+    ``all_gather_into_tensor`` of the [M, N/G] outputs (KB-scale at small M)
+    rebuilds y [M, N] on every rank, or y stays sharded (``gather=False``) for
+    a following layer that consumes channel shards. The reference has no such
+    split (its row_split.py splits tokens or the batch); this is the B200
+    re-design of §8(e)'s small-M case.
+
+    ``local_forward(shard, x)`` computes the local slice; it defaults to the
+    shard module's own forward (the CUDA kernels).
+    """
+
+    def __init__(self, linear, group=None, local_forward=None):
+        super().__init__()
+        from .ops import Gfx906Int4Ops
+        if not getattr(linear, "quantized", False):
+            raise ValueError("the channel split takes a quantized Gfx906Int4Ops.Linear")
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.out_features = linear.out_features
+        n0, n1 = channel_block(linear.out_features, self.rank, self.world)
+        dev = linear.weight_q4.device
+        dtype = linear.bias.dtype if linear.bias is not None else None
+        shard = Gfx906Int4Ops.Linear(linear.in_features, n1 - n0, bias=linear.bias is not None, device=dev,
+                                     dtype=dtype, rotation_group=linear.rotation_group)
+        with torch.no_grad():
+            shard.weight_q4.copy_(linear.weight_q4[n0:n1])
+            shard.weight_scale.copy_(linear.weight_scale[n0:n1])
+            if linear.bias is not None:
+                shard.bias.copy_(linear.bias[n0:n1])
+        self.shard = shard
+        self.local_forward = local_forward
+
+    def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        y = self.local_forward(self.shard, x) if self.local_forward is not None else self.shard(x)
+        if not gather:
+            return y
+        lead, n_local = y.shape[:-1], y.shape[-1]
+        y2 = y.reshape(-1, n_local).contiguous()
+        full = torch.empty(self.world * y2.shape[0], n_local, dtype=y2.dtype, device=y2.device)
+        dist.all_gather_into_tensor(full, y2, group=self.group)  # rank-major blocks of rows
+        full = full.view(self.world, y2.shape[0], n_local).permute(1, 0, 2).reshape(y2.shape[0], -1)
+        return full.reshape(*lead, self.world * n_local)

@@ -1,7 +1,9 @@
 """Multi-process split logic on the CPU (gloo, world size 2): the token-row and
-batch splits reproduce the single-process forward of the same DiT, and a rank
-that fails makes its peer's collective end with an error (bounded timeout)
-instead of waiting forever (reference: row_split.py:208-241)."""
+batch splits reproduce the single-process forward of the same DiT, the
+output-channel split of one int4 linear gathers the same y as the unsplit
+layer (local slices computed by the oracle), and a rank that fails makes its
+peer's collective end with an error (bounded timeout) instead of waiting
+forever (reference: row_split.py:208-241)."""
 import datetime
 import multiprocessing as mp
 import os
@@ -52,6 +54,10 @@ def _worker(rank, world, port, mode, q):
                 except Exception as e:  # the peer's collective must end with an error
                     q.put((rank, "error", type(e).__name__))
                 return
+            if mode == "channel":
+                q.put((rank, "ok", _channel_split_error(parallel)))
+                dist.destroy_process_group()
+                return
             ref = model(*inputs)
             if mode == "rows":
                 got = parallel.split_forward_rows(model, *inputs, H_TOK, W_TOK)
@@ -61,6 +67,38 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
     except Exception:
         q.put((rank, "exception", traceback.format_exc()))
+
+
+def _channel_split_error(parallel):
+    """Max relative error of the gathered channel-split output against the
+    unsplit layer, both through the oracle's W4A16 matmul (bit-identical
+    slices: the split must only move rows around)."""
+    import numpy as np
+    import oracle as O
+    from comfy_ui_gfx906_tools_b200 import ops
+    N, K, M = 96, 128, 3
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(N, K, generator=g)
+    p, s = O.quantize_pack_int4(w.numpy())
+    lin = ops.Gfx906Int4Ops.Linear(K, N, bias=True, dtype=torch.float32)
+    with torch.no_grad():
+        lin.weight_q4.copy_(torch.from_numpy(p))
+        lin.weight_scale.copy_(torch.from_numpy(s))
+        lin.bias.copy_(torch.randn(N, generator=g))
+    x = torch.randn(1, M, K, generator=g)
+
+    def oracle_forward(mod, xx):
+        y = O.w4a16_matmul(xx.reshape(-1, K).numpy(), mod.weight_q4.numpy(), mod.weight_scale.numpy(),
+                           mod.bias.detach().numpy())
+        return torch.from_numpy(np.asarray(y, dtype=np.float32)).reshape(*xx.shape[:-1], -1)
+
+    split = parallel.ChannelShardLinear(lin, local_forward=oracle_forward)
+    got = split(x)
+    ref = oracle_forward(lin, x)
+    assert got.shape == ref.shape == (1, M, N)
+    local = split(x, gather=False)
+    assert local.shape == (1, M, N // 2)
+    return float((got - ref).abs().max() / ref.abs().max())
 
 
 def _run(mode):
@@ -80,7 +118,7 @@ def _run(mode):
     return sorted(results)
 
 
-@pytest.mark.parametrize("mode", ["rows", "batch"])
+@pytest.mark.parametrize("mode", ["rows", "batch", "channel"])
 def test_split_matches_single_process(mode):
     res = _run(mode)
     for rank, status, val in res:
@@ -100,3 +138,6 @@ def test_row_block_partition():
     with pytest.raises(ValueError):
         parallel.row_block(10, 0, 4)
     assert parallel.batch_slice(8, 3, 4) == slice(6, 8)
+    assert [parallel.channel_block(96, r, 3) for r in range(3)] == [(0, 32), (32, 64), (64, 96)]
+    with pytest.raises(ValueError):
+        parallel.channel_block(10, 0, 4)
