@@ -45,6 +45,7 @@ enum DeviceErrorCode : int {
   kDevErrEmptyBarrierTimeout = 2,
   kDevErrMmaBarrierTimeout = 3,
   kDevErrEpilogueBarrierTimeout = 4,
+  kDevErrClusterReduceTimeout = 5,
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
@@ -133,6 +134,50 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Store to distributed shared memory (a mapa'd shared::cluster address).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Arrive with release at cluster scope on the barrier at the same offset in
+// CTA `rank`: this thread's earlier stores, distributed shared memory
+// included, are visible to a cluster-scope acquire of the completed phase.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   mapa_shared(smem_u32(bar), rank))
+               : "memory");
+}
+
+// Bounded wait with acquire at cluster scope (pairs with the arrive above).
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity, int code) {
+  const unsigned long long t0 = global_timer_ns();
+  uint32_t spins = 0;
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((++spins & 255u) == 0u) {
+      if (*(volatile int*)&g_device_error != 0) return false;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        record_device_error(code);
+        return false;
+      }
+    }
+  }
 }
 
 // Arrive on the barrier at the same offset in CTA `rank` of the cluster

@@ -142,7 +142,7 @@ __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
   return (int)(((t + 1) * G + U - 1) / U) - 1;
 }
 
-template <int NT, int STAGES, bool kF16Scale, typename OutT>
+template <int NT, int STAGES, bool kF16Scale, typename OutT, bool kCl>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (NT == 2 ? GFX_SMALLM_CTAS_NT2 : 1))
     w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
   uint64_t* empty = full + STAGES;
   int* s_flag = reinterpret_cast<int*>(empty + STAGES);
+  uint64_t* cl_go = empty + STAGES + 1;   // cluster split-K: "leader's ring is free" (peers)
+  uint64_t* cl_red = empty + STAGES + 2;  // cluster split-K: peers' partials landed (leader)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -175,10 +177,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
       mbar_init(&full[s], scale_tma ? 1 : 1 + 32);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    if constexpr (kCl) {
+      mbar_init(cl_go, 1);
+      mbar_init(cl_red, (cluster_nctarank() - 1) * L::kRowSlices * 32);
+    }
     fence_barrier_init();
   }
-  __syncthreads();
-  if (n_iters <= 0) return;
+  if constexpr (kCl) {
+    cluster_sync_all();  // peers' barriers are initialised before any remote arrive
+  } else {
+    __syncthreads();
+  }
+  if (!kCl && n_iters <= 0) return;  // a cluster CTA always has units (classic split)
   pdl_trigger();
 
   if (warp == kConsumerWarps) {
@@ -229,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
         cp_async_mbar_arrive_noinc(&full[stage]);
       }
     }
+    if constexpr (kCl) cluster_sync_all();  // no CTA of the cluster leaves while a peer may address it
     return;
   }
 
@@ -253,7 +264,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     const uint32_t phase = (it / STAGES) & 1;
     // A consumer that gives up here leaves early; its peers reach the same
     // wait (they all consume the same stages) and give up the same way.
-    if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) return;
+    if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) {
+      if constexpr (kCl) cluster_sync_all();
+      return;
+    }
     const uint8_t* st = smem + stage * L::kStageBytes;
     const uint32_t nib_base = smem_u32(st);
     const uint8_t* sc = st + L::kNibBytes;
@@ -417,6 +431,59 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
               }
           }
       }
+    } else if constexpr (kCl) {
+      // 2') cluster split-K: the CTAs of one row block are one cluster; rank 0
+      // (the first K segment) takes the peers' fp32 partials into its stage
+      // ring (free once its own units are consumed) through distributed shared
+      // memory, sums them in rank order (deterministic), adds the bias, stores.
+      const uint32_t rank = cluster_ctarank(), csize = cluster_nctarank();
+      constexpr int kRecvStride = kRows + 4;  // padded token rows: conflict-free reads
+      const int vt = (M - tok0) < kTok ? (M - tok0) : kTok;  // valid tokens of this token block
+      float* recv = reinterpret_cast<float*>(smem);
+      if (rank != 0) {
+        if (kq == 0 && mbar_wait_acq_cluster(cl_go, 0, kDevErrClusterReduceTimeout)) {
+          const uint32_t dst = mapa_shared(smem_u32(recv), 0) + (rank - 1) * (uint32_t)(kTok * kRecvStride * 4);
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int r = rs * 16 * kMT + mt * 16 + g_ + half * 8;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                  const int tok = nt * 8 + tok_perm(2 * t_ + cc);
+                  if (tok < vt) st_shared_cluster_f32(dst + (uint32_t)(tok * kRecvStride + r) * 4u, acc[mt][nt][half * 2 + cc]);
+                }
+            }
+          mbar_arrive_release_cluster(cl_red, 0);
+        }
+      } else {
+        consumer_sync();  // every consumer is done reading the ring (K-part reduction)
+        if (threadIdx.x == 0)
+          for (uint32_t q = 1; q < csize; ++q) mbar_arrive_release_cluster(cl_go, q);
+        if (kq == 0 && mbar_wait_acq_cluster(cl_red, 0, kDevErrClusterReduceTimeout)) {
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int r = rs * 16 * kMT + mt * 16 + g_ + half * 8;
+              const int n = n0 + r;
+              if (n >= N) continue;
+              const float bv = bias ? to_f32(bias[n]) : 0.0f;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                  const int tok = nt * 8 + tok_perm(2 * t_ + cc);
+                  if (tok >= vt) continue;
+                  float v = acc[mt][nt][half * 2 + cc];
+                  for (uint32_t q = 1; q < csize; ++q) v += recv[((q - 1) * kTok + tok) * kRecvStride + r];
+                  y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v + bv);
+                }
+            }
+        }
+      }
     } else {
       // 2) this segment's partial -> workspace slot [tb][rb][seg] ([token][row] order)
       const int seg = c - owner_cta(rb_lo, U, G);
@@ -493,6 +560,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
   }
+  if constexpr (kCl) cluster_sync_all();  // no CTA of the cluster leaves while a peer may address it
 }
 
 }  // namespace smallm
@@ -504,6 +572,7 @@ GFX_DEFINE_STATUS_READER(splitk_device_status)
 
 struct SmallMPlan {
   int nt, tok, tok_blocks, RB, KS, G, max_segs, ctas_per_sm, stages;
+  int cl;  // classic split count s when 2 <= s <= 16 (cluster split-K candidate), else 0
 };
 
 static int nt_for(int M) { return M <= 8 ? 1 : (M <= 16 ? 2 : 4); }
@@ -542,6 +611,9 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
     }
   }
   p.G = (int)G;
+  // a classic split (G = RB * s: every CTA inside one row block) can reduce
+  // through distributed shared memory when s CTAs fit in one cluster
+  p.cl = (G % p.RB == 0 && G / p.RB >= 2 && G / p.RB <= 16) ? (int)(G / p.RB) : 0;
   // segments per row block: a row block spans KS units and every CTA range
   // holds at least floor(U / G) of them
   const long long min_units = U / G;
@@ -578,21 +650,12 @@ struct SmallMArgs {
   int M, N, K;
 };
 
-template <int NT, int STAGES, bool F16S, typename OutT>
-static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st) {
+template <int NT, int STAGES, bool F16S, typename OutT, bool kCl>
+static int launch_smallm_k(const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st, int cluster) {
   using L = smallm::Layout<NT, STAGES, F16S>;
-  auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT>;
-  static bool attr_set[64] = {false};  // per device
-  const int dev = current_device();
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
-    if (e != cudaSuccess)
-      return set_error(GFX_ERR_CUDA, "w4a16_smallm: cannot set %d bytes of shared memory: %s", L::kSmemBytes,
-                       cudaGetErrorString(e));
-    attr_set[dev] = true;
-  }
+  auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, kCl>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(p.G, p.tok_blocks);
   cfg.blockDim = dim3(smallm::kThreads);
   cfg.dynamicSmemBytes = L::kSmemBytes;
@@ -601,10 +664,79 @@ static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (kCl) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
                                      (const OutT*)a.bias, (OutT*)a.y, a.part, a.cnt, a.M, a.N, a.K, p.G, p.max_segs);
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a16_smallm_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a16_smallm_kernel");
+}
+
+// Cluster split-K (opt-in, GFX906_B200_SMALLM_CLUSTER=1): a classic split s
+// (2..16) whose peers' partials fit in the leader's stage ring and whose
+// RB * token_blocks clusters can all be resident at once. On B200 it measured
+// no faster than the global fix-up at M = 1 (the vectorised fix-up is ~1 us)
+// and 2x slower for the 2-CTA clusters of the M = 16 qkv shape, so the global
+// fix-up stays the default.
+template <int NT, int STAGES, bool F16S, typename OutT>
+static bool smallm_use_cluster(const SmallMPlan& p) {
+  using L = smallm::Layout<NT, STAGES, F16S>;
+  if (p.cl < 2) return false;
+  const char* env = getenv("GFX906_B200_SMALLM_CLUSTER");
+  if (!(env && env[0] == '1' && env[1] == 0)) return false;
+  const size_t recv = (size_t)(p.cl - 1) * L::kTok * (smallm::kRows + 4) * sizeof(float);
+  if (recv > (size_t)STAGES * L::kStageBytes) return false;
+  static int max_active[64][17];  // per device and cluster size: 0 unknown, -1 impossible, else clusters
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return false;
+  int& m = max_active[dev][p.cl];
+  if (m == 0) {
+    auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true>;
+    m = -1;
+    if (p.cl > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(p.cl * 16);
+    cfg.blockDim = dim3(smallm::kThreads);
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) m = n;
+    (void)cudaGetLastError();
+  }
+  return m > 0 && (long long)m >= (long long)p.RB * p.tok_blocks;
+}
+
+template <int NT, int STAGES, bool F16S, typename OutT>
+static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st) {
+  using L = smallm::Layout<NT, STAGES, F16S>;
+  static bool attr_set[64] = {false};  // per device
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    for (auto kern : {smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, false>,
+                      smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true>}) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+      if (e != cudaSuccess)
+        return set_error(GFX_ERR_CUDA, "w4a16_smallm: cannot set %d bytes of shared memory: %s", L::kSmemBytes,
+                         cudaGetErrorString(e));
+    }
+    attr_set[dev] = true;
+  }
+  if (smallm_use_cluster<NT, STAGES, F16S, OutT>(p)) return launch_smallm_k<NT, STAGES, F16S, OutT, true>(p, a, st, p.cl);
+  return launch_smallm_k<NT, STAGES, F16S, OutT, false>(p, a, st, 1);
 }
 
 template <int NT, int STAGES, bool F16S>

@@ -69,6 +69,27 @@ def test_gemm_splits_agree(cuda, splits):
     _check(y.cpu().numpy(), ref, 1e-5, 1e-5)
 
 
+@pytest.mark.parametrize("M,N,K,splits", [(1, 3072, 3072, 0), (16, 3072, 3072, 0), (5, 1024, 4096, 4),
+                                           (9, 640, 3072, 3), (40, 384, 2048, 2), (3, 3072, 15360, 0)])
+def test_gemm_cluster_splitk_matches_global_fixup(cuda, monkeypatch, M, N, K, splits):
+    """Classic split-K plans reduce through distributed shared memory inside a
+    cluster (opt-in, GFX906_B200_SMALLM_CLUSTER=1) or through global partials;
+    both sum the K segments in the same order, so the outputs are identical
+    (zero signs aside), and both match the oracle."""
+    p, s, pd, sd = _weights(N, K, 91 + M, cuda)
+    sd16 = ops.scales_to_f16_if_exact(sd)
+    xn, xd = _x(M, K, 92 + M, cuda)
+    bias = torch.linspace(-1, 1, N, device=cuda)
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("GFX906_B200_SMALLM_CLUSTER", mode)
+        out[mode] = (ops.gemm_w4a16(xd, pd, sd16, bias, torch.float32, splits=splits) + 0.0,
+                     ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16, splits=splits).float() + 0.0)
+    monkeypatch.delenv("GFX906_B200_SMALLM_CLUSTER")
+    assert torch.equal(out["1"][0], out["0"][0]) and torch.equal(out["1"][1], out["0"][1])
+    _check(out["1"][0].cpu().numpy(), O.w4a16_matmul(xn, p, s, bias.cpu().numpy()), 1e-5, 1e-5)
+
+
 def test_gemm_deterministic_and_workspace_rearmed(cuda):
     N, K, M = 512, 6144, 5
     p, s, pd, sd = _weights(N, K, 3, cuda)
