@@ -126,7 +126,7 @@ int gfx_device_status(int clear) {
   int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return -set_error(GFX_ERR_CUDA, "gfx_device_status: %s", cudaGetErrorString(e));
-  const int parts[2] = {splitk_device_status(clear), tc_device_status(clear)};
+  const int parts[3] = {splitk_device_status(clear), tc_device_status(clear), selftest_device_status(clear)};
   for (int p : parts) {
     if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
     if (p && !v) v = p;

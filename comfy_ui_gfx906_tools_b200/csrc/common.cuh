@@ -46,6 +46,7 @@ enum DeviceErrorCode : int {
   kDevErrMmaBarrierTimeout = 3,
   kDevErrEpilogueBarrierTimeout = 4,
   kDevErrClusterReduceTimeout = 5,
+  kDevErrSelfTestTimeout = 6,  // gfx_selftest_wait_timeout: the expected outcome
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
@@ -96,22 +97,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code`) once the timeout passes,
+// Bounded wait: returns false (and records `code`) once `timeout_ns` passes,
 // or at once if another thread of the grid already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int code,
+                                              unsigned long long timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0u) {
       if (*(volatile int*)&g_device_error != 0) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > timeout_ns) {
         record_device_error(code);
         return false;
       }
     }
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  return mbar_wait_for(bar, parity, code, kWaitTimeoutNs);
 }
 
 // ---------------------------------------------------------------------------

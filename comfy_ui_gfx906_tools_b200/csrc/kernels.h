@@ -28,6 +28,7 @@ int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dty
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 bool w4a16_tc_supported(int M, int N, int K, int scale_dtype);
 int tc_device_status(int clear);
+int selftest_device_status(int clear);
 int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 

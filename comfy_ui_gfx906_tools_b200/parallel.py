@@ -24,10 +24,23 @@ thread barrier, row_split.py:220-240).
 """
 from __future__ import annotations
 
+import logging
+
 import torch
 import torch.distributed as dist
 
 from .flux_dit import AttentionExchange
+
+_log = logging.getLogger(__name__)
+_last_plan = {}
+
+
+def _log_plan(kind: str, **plan):
+    """One "[Gfx906 Split]" line whenever a split's plan changes (row_split.py:130-133)."""
+    key = tuple(sorted(plan.items()))
+    if _last_plan.get(kind) != key:
+        _last_plan[kind] = key
+        _log.info("[Gfx906 Split] %s %s", kind, ", ".join(f"{k}={v}" for k, v in key))
 
 
 class TokenShard(AttentionExchange):
@@ -63,6 +76,7 @@ def split_forward_rows(model, img, img_ids, txt, txt_ids, timesteps, y, h_tokens
     the full [B, L_img, C] output on every rank (or the local rows)."""
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     r0, r1 = row_block(h_tokens, rank, world)
+    _log_plan("rows", world=world, rank=rank, latent_rows=f"{r0}:{r1}", h_tokens=h_tokens, w_tokens=w_tokens)
     sl = slice(r0 * w_tokens, r1 * w_tokens)
     saved = model.exchange
     model.exchange = TokenShard(group)
@@ -90,6 +104,7 @@ def split_forward_batch(model, img, img_ids, txt, txt_ids, timesteps, y, group=N
     full output on every rank (or the local slice)."""
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     sl = batch_slice(img.shape[0], rank, world)
+    _log_plan("batch", world=world, rank=rank, samples=f"{sl.start}:{sl.stop}", batch=img.shape[0])
     out = model(img[sl], img_ids[sl], txt[sl], txt_ids[sl], timesteps[sl], y[sl])
     if not gather_output:
         return out
@@ -131,6 +146,7 @@ class ChannelShardLinear(torch.nn.Module):
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.out_features = linear.out_features
         n0, n1 = channel_block(linear.out_features, self.rank, self.world)
+        _log_plan("channels", world=self.world, rank=self.rank, channels=f"{n0}:{n1}", out_features=linear.out_features)
         dev = linear.weight_q4.device
         dtype = linear.bias.dtype if linear.bias is not None else None
         shard = Gfx906Int4Ops.Linear(linear.in_features, n1 - n0, bias=linear.bias is not None, device=dev,

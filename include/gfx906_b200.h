@@ -58,6 +58,13 @@ int gfx_version(void);
  * resets the word to 0. */
 int gfx_device_status(int clear);
 
+/* Failure-detection check (no reference counterpart; used by the tests): one
+ * CTA waits on an mbarrier nothing arrives on, gives up after timeout_us
+ * (0 < timeout_us <= 1e6) and records status code 6 in the device status
+ * word, exactly as a stuck GEMM pipeline would; the context stays usable.
+ * Returns 0 once launched; read the outcome with gfx_device_status. */
+int gfx_selftest_wait_timeout(int timeout_us, void* stream);
+
 /*
  * W4A16 GEMM:  y[M, N] = x[M, K] @ dequant(w_q4, w_scale)^T (+ bias)
  *

@@ -88,3 +88,10 @@ def test_error_message_is_thread_local(built_lib):
     t.join()
     assert msgs["t"] == ""
     assert "K % 32" in _lib.last_error()
+
+
+def test_selftest_rejects_bad_budget(built_lib):
+    # argument check only: nothing is launched
+    assert built_lib.gfx_selftest_wait_timeout(0, None) == 1
+    assert built_lib.gfx_selftest_wait_timeout(2_000_000, None) == 1
+    assert b"timeout_us" in built_lib.gfx_last_error()

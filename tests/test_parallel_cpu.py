@@ -45,6 +45,16 @@ def _worker(rank, world, port, mode, q):
         torch.set_num_threads(2)
         model, inputs = _model_and_inputs()
         with torch.no_grad():
+            if mode == "fail_after":
+                parallel.split_forward_rows(model, *inputs, H_TOK, W_TOK)  # one full exchange succeeds
+                if rank == 1:
+                    raise RuntimeError("rank 1 failed after an exchange")
+                try:
+                    parallel.split_forward_rows(model, *inputs, H_TOK, W_TOK)
+                    q.put((rank, "no-error", None))
+                except Exception as e:
+                    q.put((rank, "error", type(e).__name__))
+                return
             if mode == "fail":
                 if rank == 1:
                     raise RuntimeError("rank 1 failed before the exchange")
@@ -126,8 +136,9 @@ def test_split_matches_single_process(mode):
         assert val < 1e-5, (rank, val)
 
 
-def test_failed_rank_surfaces_as_error():
-    res = dict((r, (s, v)) for r, s, v in _run("fail"))
+@pytest.mark.parametrize("mode", ["fail", "fail_after"])
+def test_failed_rank_surfaces_as_error(mode):
+    res = dict((r, (s, v)) for r, s, v in _run(mode))
     assert res[1][0] == "exception" and "rank 1 failed" in res[1][1]
     assert res[0][0] == "error", res[0]
 
