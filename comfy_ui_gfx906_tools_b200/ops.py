@@ -363,6 +363,27 @@ def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, 
     return out.reshape(*shape[:-1], w_packed.shape[0])
 
 
+def int4_linear_w4a4(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                     rotation_group: int = 0) -> torch.Tensor:
+    """The reference's own ``int4_linear`` numerics (ops.py:167-183): the
+    activation is quantized to int4 per 32-block with ``quantize_int4``
+    (bit-exact with the reference's quantizer, int4_gemm_scaled.hip:197-220)
+    before the GEMM. The codes are dequantized exactly to bf16 (one rounding of
+    code * scale) and multiplied with the bf16 weights on the W4A16 path, so
+    the result equals the reference's integer-block GEMM up to those two bf16
+    roundings, not bit for bit."""
+    shape = x.shape
+    K = shape[-1]
+    x2d = x.reshape(-1, K)
+    if rotation_group:
+        R = get_group_rotation(K, rotation_group, x2d.device)
+        x2d = apply_group_rotation(x2d.float(), R, rotation_group)
+    pa, sa = quantize_int4(x2d.contiguous())
+    xq = dequantize_int4(pa, sa, torch.bfloat16)
+    out = gemm_w4a16(xq, w_packed, w_scale, bias, x.dtype)
+    return out.reshape(*shape[:-1], w_packed.shape[0])
+
+
 # ---------------------------------------------------------------------------
 # custom_operations integration (reference ops.py:186-276)
 # ---------------------------------------------------------------------------
@@ -399,6 +420,9 @@ class Gfx906Int4Ops(_OpsBase):
 
         quantize_device = None
         quantized_on_load = 0
+        # True: the reference's W4A4 numerics (int4_linear_w4a4) instead of
+        # the weight-only W4A16 product
+        activation_quant = False
 
         def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
                                   error_msgs):
@@ -442,6 +466,8 @@ class Gfx906Int4Ops(_OpsBase):
             if weight_scale is self.weight_scale:
                 weight_scale = self._device_scale(weight_scale)
             bias = self.bias.to(x.device, x.dtype) if self.bias is not None else None
+            if self.activation_quant:
+                return int4_linear_w4a4(x, weight_q4, weight_scale, bias, self.rotation_group)
             return int4_linear(x, weight_q4, weight_scale, bias, self.rotation_group)
 
 
