@@ -243,4 +243,17 @@ int scales_to_f16(const float* scale, void* scale_f16, int64_t n, int* inexact, 
   return launch_scales_to_f16(scale, scale_f16, n, inexact, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int hadamard_rotate(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t rows, int K,
+                    int group, gfx_stream_t stream) {
+  if (group != 32 && group != 64 && group != 128)
+    return set_error(GFX_ERR_INVALID, "hadamard_rotate: group must be 32, 64 or 128, got %d", group);
+  if (rows < 0 || K <= 0 || K % group != 0)
+    return set_error(GFX_ERR_INVALID, "hadamard_rotate: K (%d) must be a positive multiple of group %d", K, group);
+  if (x_dtype < 0 || x_dtype > 2 || out_dtype < 0 || out_dtype > 2)
+    return set_error(GFX_ERR_INVALID, "hadamard_rotate: dtype codes must be 0, 1 or 2");
+  if (rows == 0) return GFX_OK;
+  if (!x || !sign || !out) return set_error(GFX_ERR_INVALID, "hadamard_rotate: null pointer");
+  return gfx::launch_hadamard_rotate(x, x_dtype, sign, out, out_dtype, rows, K, group, (cudaStream_t)stream);
+}
+
 }  // extern "C"

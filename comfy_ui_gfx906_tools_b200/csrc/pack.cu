@@ -227,4 +227,86 @@ int launch_scales_to_f16(const float* s, void* s16, int64_t n, int* inexact, cud
   return check_launch("scales_to_f16_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// block-diagonal randomized Hadamard rotation of activations
+// ---------------------------------------------------------------------------
+// out[r, g*G + i] = sum_j H_G[i, j] * sign[j] * x[r, g*G + j] / sqrt(G): the
+// reference's `flat @ R^T` with R = H_G / sqrt(G) * diag(sign)
+// (ops.py:68-105), evaluated as a fast Walsh-Hadamard transform instead of a
+// G x G matmul: one warp per (row, group), E = G/32 consecutive elements per
+// lane; butterflies of stride < E stay in registers, wider ones exchange
+// through warp shuffles. fp32 arithmetic; the summation order differs from a
+// matmul, so results agree with it to fp32 rounding, not bit for bit.
+template <int E, typename InT, typename OutT>
+__global__ void hadamard_rotate_kernel(const InT* __restrict__ x, const float* __restrict__ sign,
+                                       OutT* __restrict__ out, int64_t items, int K) {
+  constexpr int G = 32 * E;
+  const int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (item >= items) return;  // whole warps leave together (items are per warp)
+  const int64_t groups_per_row = K / G;
+  const int64_t row = item / groups_per_row, g = item % groups_per_row;
+  const int64_t base = row * K + g * G + lane * E;
+  float v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = to_f32(x[base + e]) * sign[lane * E + e];
+  // strides inside a lane's E elements
+#pragma unroll
+  for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      if ((e & h) == 0) {
+        const float a = v[e], b = v[e + h];
+        v[e] = a + b;
+        v[e + h] = a - b;
+      }
+    }
+  }
+  // strides across lanes: element index bit h*E <-> lane bit h
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[e], h);
+      v[e] = upper ? other - v[e] : v[e] + other;
+    }
+  }
+  const float norm = rsqrtf((float)G);
+#pragma unroll
+  for (int e = 0; e < E; ++e) out[base + e] = from_f32<OutT>(v[e] * norm);
+}
+
+template <int E, typename InT>
+static int launch_hadamard_in(const void* x, const float* sign, void* out, int out_dtype, int64_t items, int K,
+                              cudaStream_t st) {
+  const int threads = 256;
+  const int64_t blocks = (items * 32 + threads - 1) / threads;
+  if (out_dtype == GFX_DTYPE_F32)
+    hadamard_rotate_kernel<E, InT, float><<<blocks, threads, 0, st>>>((const InT*)x, sign, (float*)out, items, K);
+  else if (out_dtype == GFX_DTYPE_F16)
+    hadamard_rotate_kernel<E, InT, __half><<<blocks, threads, 0, st>>>((const InT*)x, sign, (__half*)out, items, K);
+  else
+    hadamard_rotate_kernel<E, InT, __nv_bfloat16>
+        <<<blocks, threads, 0, st>>>((const InT*)x, sign, (__nv_bfloat16*)out, items, K);
+  return check_launch("hadamard_rotate_kernel");
+}
+
+template <int E>
+static int launch_hadamard_e(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t items,
+                             int K, cudaStream_t st) {
+  if (x_dtype == GFX_DTYPE_F32) return launch_hadamard_in<E, float>(x, sign, out, out_dtype, items, K, st);
+  if (x_dtype == GFX_DTYPE_F16) return launch_hadamard_in<E, __half>(x, sign, out, out_dtype, items, K, st);
+  return launch_hadamard_in<E, __nv_bfloat16>(x, sign, out, out_dtype, items, K, st);
+}
+
+int launch_hadamard_rotate(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t rows,
+                           int K, int group, cudaStream_t stream) {
+  const int64_t items = rows * (K / group);
+  if (items == 0) return GFX_OK;
+  if (group == 32) return launch_hadamard_e<1>(x, x_dtype, sign, out, out_dtype, items, K, stream);
+  if (group == 64) return launch_hadamard_e<2>(x, x_dtype, sign, out, out_dtype, items, K, stream);
+  return launch_hadamard_e<4>(x, x_dtype, sign, out, out_dtype, items, K, stream);
+}
+
 }  // namespace gfx

@@ -103,15 +103,44 @@ def choose_rotation_group(in_features: int, max_group: int = 128, min_group: int
     return None
 
 
+def rotation_signs(group: int, device) -> torch.Tensor:
+    """The +-1 float vector of get_group_rotation: a CPU generator seeded
+    ROTATION_SEED ^ group (ops.py:68-82)."""
+    key = ("signs", group, str(device))
+    if key not in _ROTATION_CACHE:
+        g = torch.Generator(device="cpu").manual_seed(ROTATION_SEED ^ group)
+        _ROTATION_CACHE[key] = (torch.randint(0, 2, (group,), generator=g).float() * 2 - 1).to(device)
+    return _ROTATION_CACHE[key]
+
+
 def get_group_rotation(in_features: int, group: int, device) -> torch.Tensor:
     """R = H_group * diag(random signs), signs from a CPU generator seeded
     ROTATION_SEED ^ group (ops.py:68-82), so folding time and forward time agree."""
     key = (in_features, group, str(device))
     if key not in _ROTATION_CACHE:
-        g = torch.Generator(device="cpu").manual_seed(ROTATION_SEED ^ group)
-        signs = (torch.randint(0, 2, (group,), generator=g).float() * 2 - 1).to(device)
-        _ROTATION_CACHE[key] = _hadamard(group, device) * signs
+        _ROTATION_CACHE[key] = _hadamard(group, device) * rotation_signs(group, device)
     return _ROTATION_CACHE[key]
+
+
+def hadamard_rotate(x: torch.Tensor, group: int, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Forward-time activation rotation on the GPU: every group-sized chunk of
+    the last dim of x (CUDA) is multiplied by R = H / sqrt(group) * diag(signs)
+    as a fast Walsh-Hadamard transform (one kernel, fp32 math, written
+    straight in out_dtype); equal to ``apply_group_rotation`` up to fp32
+    rounding."""
+    _require_cuda(x, "x")
+    shape = x.shape
+    K = shape[-1]
+    src = x.reshape(-1, K)
+    if src.dtype not in _DTYPE_CODE:
+        src = src.float()
+    src = src.contiguous()
+    out = torch.empty(src.shape, dtype=out_dtype, device=x.device)
+    sign = rotation_signs(group, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("hadamard_rotate", src.data_ptr(), _dtype_code(src.dtype), sign.data_ptr(), out.data_ptr(),
+                  _dtype_code(out_dtype), src.shape[0], K, group, _stream(x.device))
+    return out.reshape(shape)
 
 
 def apply_group_rotation(t: torch.Tensor, R: torch.Tensor, group: int) -> torch.Tensor:
@@ -357,8 +386,7 @@ def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, 
     K = shape[-1]
     x2d = x.reshape(-1, K)
     if rotation_group:
-        R = get_group_rotation(K, rotation_group, x2d.device)
-        x2d = apply_group_rotation(x2d.float(), R, rotation_group)
+        x2d = hadamard_rotate(x2d, rotation_group, torch.bfloat16)  # the GEMM's bf16 operand, one pass
     out = gemm_w4a16(x2d, w_packed, w_scale, bias, x.dtype)
     return out.reshape(*shape[:-1], w_packed.shape[0])
 
@@ -376,8 +404,7 @@ def int4_linear_w4a4(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Ten
     K = shape[-1]
     x2d = x.reshape(-1, K)
     if rotation_group:
-        R = get_group_rotation(K, rotation_group, x2d.device)
-        x2d = apply_group_rotation(x2d.float(), R, rotation_group)
+        x2d = hadamard_rotate(x2d, rotation_group, torch.float32)  # fp32, as the reference quantizes
     pa, sa = quantize_int4(x2d.contiguous())
     xq = dequantize_int4(pa, sa, torch.bfloat16)
     out = gemm_w4a16(xq, w_packed, w_scale, bias, x.dtype)

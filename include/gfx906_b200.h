@@ -163,6 +163,17 @@ int int4_dequant(const void* w_q4, const void* w_scale, int scale_dtype, void* o
  * the round trip exactly (*inexact, a device int, is overwritten). */
 int scales_to_f16(const float* scale, void* scale_f16, int64_t n, int* inexact, gfx_stream_t stream);
 
+/* Block-diagonal randomized Hadamard rotation of activations (the forward
+ * half of rotation_group != 0 in int4_linear, ops.py:85-105,176-179):
+ *   out[r, g*group + i] = sum_j H[i, j] * sign[j] * x[r, g*group + j] / sqrt(group)
+ * with H the Sylvester Hadamard matrix of order group (32, 64 or 128) and
+ * sign[group] the float +-1 vector of get_group_rotation. x, out [rows, K]
+ * (K % group == 0), dtype codes 0/1/2; out may not alias x. Computed as a
+ * fast Walsh-Hadamard transform in fp32, equal to the reference's fp32
+ * matmul up to fp32 rounding. */
+int hadamard_rotate(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t rows, int K,
+                    int group, gfx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

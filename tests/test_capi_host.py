@@ -95,3 +95,11 @@ def test_selftest_rejects_bad_budget(built_lib):
     assert built_lib.gfx_selftest_wait_timeout(0, None) == 1
     assert built_lib.gfx_selftest_wait_timeout(2_000_000, None) == 1
     assert b"timeout_us" in built_lib.gfx_last_error()
+
+
+def test_hadamard_rotate_argument_checks(built_lib):
+    # argument checks only: nothing is launched
+    assert built_lib.hadamard_rotate(None, 0, None, None, 0, 4, 96, 48, None) == 1
+    assert b"group" in built_lib.gfx_last_error()
+    assert built_lib.hadamard_rotate(None, 0, None, None, 0, 4, 96, 64, None) == 1
+    assert built_lib.hadamard_rotate(None, 0, None, None, 0, 0, 128, 64, None) == 0  # rows == 0: no-op
