@@ -243,6 +243,17 @@ int scales_to_f16(const float* scale, void* scale_f16, int64_t n, int* inexact, 
   return launch_scales_to_f16(scale, scale_f16, n, inexact, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int repack_q8_0(const void* raw, void* q, float* scale, int N, int K, gfx_stream_t stream) {
+  if (N < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "repack_q8_0: expected N >= 0 and K a positive multiple of 32, got [%d, %d]", N,
+                     K);
+  if (N == 0) return GFX_OK;
+  if (!raw || !q || !scale) return set_error(GFX_ERR_INVALID, "repack_q8_0: null pointer");
+  if (((uintptr_t)raw & 1) || ((uintptr_t)q & 15))
+    return set_error(GFX_ERR_INVALID, "repack_q8_0: raw must be 2-byte and q 16-byte aligned");
+  return gfx::launch_repack_q8_0(raw, q, scale, N, K, (cudaStream_t)stream);
+}
+
 int hadamard_rotate(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t rows, int K,
                     int group, gfx_stream_t stream) {
   if (group != 32 && group != 64 && group != 128)

@@ -42,6 +42,7 @@ int launch_quantize_pack_int4(const void* x, int x_dtype, void* packed, float* s
 int launch_quantize_int8(const void* x, int x_dtype, void* q, float* scale, int64_t rows, int K,
                          cudaStream_t stream);
 int launch_scales_to_f16(const float* s, void* s16, int64_t n, int* inexact, cudaStream_t stream);
+int launch_repack_q8_0(const void* raw, void* q, float* scale, int N, int K, cudaStream_t stream);
 int launch_hadamard_rotate(const void* x, int x_dtype, const float* sign, void* out, int out_dtype, int64_t rows,
                            int K, int group, cudaStream_t stream);
 

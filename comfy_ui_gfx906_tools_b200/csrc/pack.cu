@@ -109,6 +109,36 @@ int launch_repack_q4_0(const void* raw, void* packed, float* scale, void* scale_
 }
 
 // ---------------------------------------------------------------------------
+// Q8_0 repack: one thread per 34-byte ggml block (fp16 d + 32 int8 codes)
+// ---------------------------------------------------------------------------
+// value = q * d: the int8 codes are already the W8A16 weight, d becomes its
+// fp32 group scale. Lossless; blocks start on even addresses (34-byte stride),
+// so the codes are read as 16 halfwords and written as two 16-byte stores.
+__global__ void repack_q8_0_kernel(const uint16_t* __restrict__ raw, uint4* __restrict__ q,
+                                   float* __restrict__ scale, int64_t blocks) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= blocks) return;
+  const uint16_t* src = raw + b * 17;
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = (uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16);
+  q[2 * b] = make_uint4(w[0], w[1], w[2], w[3]);
+  q[2 * b + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+  __half_raw hr;
+  hr.x = src[0];
+  scale[b] = __half2float(__half(hr));
+}
+
+int launch_repack_q8_0(const void* raw, void* q, float* scale, int N, int K, cudaStream_t stream) {
+  const int64_t blocks = (int64_t)N * (K / 32);
+  if (blocks == 0) return GFX_OK;
+  const int threads = 256;
+  repack_q8_0_kernel<<<(unsigned)((blocks + threads - 1) / threads), threads, 0, stream>>>(
+      (const uint16_t*)raw, (uint4*)q, scale, blocks);
+  return check_launch("repack_q8_0_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // block-32 quantizers: one thread per block
 // ---------------------------------------------------------------------------
 template <typename T>

@@ -214,6 +214,32 @@ def repack_q4_0_native(raw_bytes: torch.Tensor, out_features: int, in_features: 
     return packed, scale
 
 
+def repack_q8_0(raw_bytes: torch.Tensor, out_features: int, in_features: int, block: int = BLOCK):
+    """Lossless ggml Q8_0 -> (int8 [N, K], float32 block scales [N, K/32]), the
+    format ``gemm_w8a16`` takes, as a GPU kernel (value = q * d). Returns
+    tensors on raw_bytes' device. The reference instead dequantizes Q8_0 and
+    re-quantizes it to int4 (nodes.py:294-301), which is lossy."""
+    if block != BLOCK:
+        raise RuntimeError(f"block must be {BLOCK}, got {block}")
+    if in_features % block != 0:
+        raise RuntimeError(f"in_features {in_features} must be a multiple of {block}")
+    nbytes = out_features * (in_features // block) * 34
+    raw = raw_bytes.reshape(-1).view(torch.uint8)
+    if raw.numel() != nbytes:
+        raise RuntimeError(f"expected {nbytes} Q8_0 bytes for [{out_features}, {in_features}], got {raw.numel()}")
+    on_cpu = not raw.is_cuda
+    dev = torch.device("cuda", torch.cuda.current_device()) if on_cpu else raw.device
+    raw = raw.to(dev).contiguous()
+    q = torch.empty(out_features, in_features, dtype=torch.int8, device=dev)
+    scale = torch.empty(out_features, in_features // block, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("repack_q8_0", raw.data_ptr(), q.data_ptr(), scale.data_ptr(), out_features, in_features,
+                  _stream(dev))
+    if on_cpu:
+        q, scale = q.cpu(), scale.cpu()
+    return q, scale
+
+
 def dequantize_int4(w_packed: torch.Tensor, w_scale: torch.Tensor, out_dtype: torch.dtype = torch.float32):
     """Dequantize native int4 weights on the GPU: code * scale as one fp32
     multiply, rounded once to out_dtype (int4_train_test.py:46-52; bf16 out

@@ -152,6 +152,14 @@ int quantize_int8(const void* x, int x_dtype, void* q, float* scale, int64_t row
  *           (either scale pointer may be NULL). */
 int repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, int N, int K, gfx_stream_t stream);
 
+/* Lossless ggml Q8_0 -> int8 weight repack (no reference kernel: the
+ * reference dequantizes Q8_0 GGUF tensors and re-quantizes them to int4,
+ * nodes.py:294-301; its GGUF report names a lossless Q8_0 repack onto the int8
+ * path as the follow-up). raw: N*(K/32) blocks of 34 bytes (fp16 d, 32 int8
+ * codes), 2-byte aligned; q int8 [N, K] (16-byte aligned) and scale float32
+ * [N, K/32] = d: exactly the block-scale int8 format w8a16_gemm reads. */
+int repack_q8_0(const void* raw, void* q, float* scale, int N, int K, gfx_stream_t stream);
+
 /* Dequantize packed int4 weights: out[N, K] = code * scale, computed as one
  * fp32 multiply and, for out_dtype bf16/f16, rounded to nearest-even once
  * (int4_train_test.py:46-52; nodes.py:51-52). The bf16 output is the exact

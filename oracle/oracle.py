@@ -37,6 +37,7 @@ __all__ = [
     "quantize_dequantize_int4", "build_q4_0_bytes", "w4a16_matmul", "quantize_int8",
     "dequant_int8", "w8a16_matmul", "parity_metrics", "unpack_int4_codes", "pack_int4_codes",
     "torch_cpu_dequant", "torch_cpu_w4a16", "w4a16_matmul_bf16w", "w4a4_matmul",
+    "build_q8_0_bytes", "repack_q8_0",
 ]
 
 
@@ -150,6 +151,26 @@ def build_q4_0_bytes(u: np.ndarray, d_f16: np.ndarray, block: int = BLOCK) -> np
     out[:, :2] = np.asarray(d_f16, dtype=np.float16).reshape(N * nb, 1).view(np.uint8).reshape(N * nb, 2)
     out[:, 2:] = (ub[:, : block // 2] & 0xF) | ((ub[:, block // 2:] & 0xF) << 4)
     return out.reshape(-1)
+
+
+def build_q8_0_bytes(q: np.ndarray, d_f16: np.ndarray, block: int = BLOCK) -> np.ndarray:
+    """ggml Q8_0 blocks (third-party format, ggml's ``block_q8_0``: fp16 d then
+    32 int8 codes, value = q * d) from int8 codes q [N, K] and fp16 d [N, K/32]."""
+    N, K = q.shape
+    nb = K // block
+    out = np.empty((N, nb, 2 + block), dtype=np.uint8)
+    out[:, :, :2] = np.asarray(d_f16, np.float16).reshape(N, nb, 1).view(np.uint8).reshape(N, nb, 2)
+    out[:, :, 2:] = np.asarray(q, np.int8).reshape(N, nb, block).view(np.uint8)
+    return out.reshape(-1)
+
+
+def repack_q8_0(raw: np.ndarray, out_features: int, in_features: int, block: int = BLOCK):
+    """Q8_0 bytes -> (int8 [N, K], float32 [N, K/32] = d), lossless."""
+    nb = in_features // block
+    b = np.asarray(raw, np.uint8).reshape(out_features, nb, 2 + block)
+    d = b[:, :, :2].copy().view(np.float16).reshape(out_features, nb).astype(np.float32)
+    q = b[:, :, 2:].copy().view(np.int8).reshape(out_features, in_features)
+    return q, d
 
 
 def dequant_int4(packed: np.ndarray, scale: np.ndarray, block: int = BLOCK) -> np.ndarray:
