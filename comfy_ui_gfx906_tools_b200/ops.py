@@ -417,6 +417,74 @@ def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, 
     return out.reshape(*shape[:-1], w_packed.shape[0])
 
 
+def gemm_int4(A_packed: torch.Tensor, A_scale: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor,
+              bias: torch.Tensor | None, out_dtype: torch.dtype, splits: int = 0, qblock: int = 32) -> torch.Tensor:
+    """The reference's block-scaled int4 GEMM op (``ext.gemm_int4``,
+    binding.cpp:73-112), same arguments, checks and messages: A_packed /
+    A_scale from ``quantize_int4`` (int4 activations), B the packed weight.
+    The A codes are dequantized exactly to bf16 (one rounding of code * scale)
+    and multiplied on the W4A16 kernels; the result matches the reference's
+    integer-block GEMM within bf16 rounding. qblock=16
+    (16-element scale blocks) is not supported by these kernels (their weight
+    groups are 32 elements) and raises."""
+    if not (A_packed.is_cuda and B_packed.is_cuda):
+        raise RuntimeError("inputs must be on device")
+    if A_packed.device != B_packed.device:
+        raise RuntimeError("A and B must be on the same device")
+    if A_packed.dtype != torch.int8 or B_packed.dtype != torch.int8:
+        raise RuntimeError("packed tensors must be int8")
+    if not (A_packed.dim() == 2 and B_packed.dim() == 2 and A_packed.shape[1] == B_packed.shape[1]
+            and A_packed.shape[1] % 16 == 0):
+        raise RuntimeError(f"expected A [M, K/2], B [N, K/2], K % 32 == 0; got A {tuple(A_packed.shape)} "
+                           f"B {tuple(B_packed.shape)}")
+    if A_scale.dtype != torch.float32 or B_scale.dtype != torch.float32:
+        raise RuntimeError("scales must be float32")
+    if qblock not in (32, 16):
+        raise RuntimeError(f"qblock must be 32 or 16, got {qblock}")
+    M, N, K = A_packed.shape[0], B_packed.shape[0], A_packed.shape[1] * 2
+    if A_scale.numel() != M * K // qblock or B_scale.numel() != N * K // qblock:
+        raise RuntimeError(f"scales must be [M, K/{qblock}] / [N, K/{qblock}] = {M * K // qblock} / "
+                           f"{N * K // qblock} elements, got {A_scale.numel()} / {B_scale.numel()}")
+    if qblock != 32:
+        raise RuntimeError("qblock=16 is not supported by the B200 kernels (32-element weight groups)")
+    if splits < 0 or splits > 16:
+        raise RuntimeError(f"splits must be in [0, 16], got {splits}")
+    if M == 0:
+        return torch.empty(0, N, dtype=out_dtype, device=A_packed.device)
+    xa = dequantize_int4(A_packed.contiguous(), A_scale.reshape(M, K // 32).contiguous(), torch.bfloat16)
+    return gemm_w4a16(xa, B_packed, B_scale.reshape(N, K // 32), bias, out_dtype, splits=splits)
+
+
+def gemm_int8(A: torch.Tensor, A_scale: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
+              bias: torch.Tensor | None, out_dtype: torch.dtype, config: int = 0) -> torch.Tensor:
+    """The reference's block-scaled int8 GEMM op (``ext.gemm_int8``,
+    binding.cpp:190-217), same arguments and checks: A / A_scale from
+    ``quantize_int8`` (int8 activations), B int8 [N, K] with float32 block
+    scales [N, K/32]. The A codes times their block scales are rounded once to
+    bf16 and multiplied on the W8A16 tensor-core kernel, matching the
+    reference's integer-block GEMM within bf16 rounding. ``config`` (the
+    reference's gfx906 tile choice) is checked and otherwise unused."""
+    if not (A.is_cuda and B.is_cuda):
+        raise RuntimeError("inputs must be on device")
+    if config < 0 or config > 3:
+        raise RuntimeError(f"config must be in [0, 3], got {config}")
+    if A.device != B.device:
+        raise RuntimeError("A and B must be on the same device")
+    if A.dtype != torch.int8 or B.dtype != torch.int8:
+        raise RuntimeError("A and B must be int8")
+    if not (A.dim() == 2 and B.dim() == 2 and A.shape[1] == B.shape[1] and A.shape[1] % 32 == 0):
+        raise RuntimeError(f"expected A [M, K], B [N, K], K % 32 == 0; got A {tuple(A.shape)} B {tuple(B.shape)}")
+    M, N, K = A.shape[0], B.shape[0], A.shape[1]
+    if A_scale.dtype != torch.float32 or B_scale.dtype != torch.float32:
+        raise RuntimeError("scales must be float32")
+    if A_scale.numel() != M * (K // 32) or B_scale.numel() != N * (K // 32):
+        raise RuntimeError(f"scales must be [M, K/32] / [N, K/32], got {tuple(A_scale.shape)} / {tuple(B_scale.shape)}")
+    if M == 0:
+        return torch.empty(0, N, dtype=out_dtype, device=A.device)
+    xa = (A.float().reshape(M, K // 32, 32) * A_scale.reshape(M, K // 32, 1)).reshape(M, K).to(torch.bfloat16)
+    return gemm_w8a16(xa, B, B_scale.reshape(N, K // 32), bias, out_dtype)
+
+
 def int4_linear_w4a4(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                      rotation_group: int = 0) -> torch.Tensor:
     """The reference's own ``int4_linear`` numerics (ops.py:167-183): the

@@ -36,7 +36,7 @@ __all__ = [
     "quantize_pack_int4", "repack_q4_0_native", "dequant_int4", "dequant_int4_bf16_bits",
     "quantize_dequantize_int4", "build_q4_0_bytes", "w4a16_matmul", "quantize_int8",
     "dequant_int8", "w8a16_matmul", "parity_metrics", "unpack_int4_codes", "pack_int4_codes",
-    "torch_cpu_dequant", "torch_cpu_w4a16", "w4a16_matmul_bf16w", "w4a4_matmul",
+    "torch_cpu_dequant", "torch_cpu_w4a16", "w4a16_matmul_bf16w", "w4a4_matmul", "block_int_matmul",
     "build_q8_0_bytes", "repack_q8_0",
 ]
 
@@ -250,6 +250,30 @@ def w4a16_matmul_bf16w(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bia
     return y
 
 
+def block_int_matmul(ca: np.ndarray, sa: np.ndarray, cb: np.ndarray, sb: np.ndarray, bias=None,
+                     block: int = BLOCK) -> np.ndarray:
+    """The reference's block-scaled integer GEMM (gemm_int4 and gemm_int8:
+    int4_gemm_scaled.hip:147-152, int8_gemm.hip:190-194): integer codes
+    ca [M, K], cb [N, K], fp32 block scales sa [M, K/block], sb [N, K/block];
+    per block the exact integer dot product, ``acc = fmaf(dot, sa * sb, acc)``
+    in block order (one split), then + bias."""
+    ca = np.asarray(ca).astype(np.int64)
+    cb = np.asarray(cb).astype(np.int64)
+    M, K = ca.shape
+    N = cb.shape[0]
+    nb = K // block
+    dots = np.einsum("mbk,nbk->mnb", ca.reshape(M, nb, block), cb.reshape(N, nb, block))  # exact integers
+    sab = (np.asarray(sa, np.float32).reshape(M, nb)[:, None, :] *
+           np.asarray(sb, np.float32).reshape(N, nb)[None, :, :]).astype(np.float32)
+    acc = np.zeros((M, N), dtype=np.float32)
+    for b in range(nb):  # fmaf: exact product + sum in float64, one rounding to float32
+        acc = (dots[:, :, b].astype(np.float64) * sab[:, :, b].astype(np.float64) + acc.astype(np.float64)).astype(
+            np.float32)
+    if bias is not None:
+        acc = acc + np.asarray(bias, dtype=np.float32)
+    return acc
+
+
 def w4a4_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None, block: int = BLOCK) -> np.ndarray:
     """The reference's production ``Linear.forward`` numerics (W4A4): the
     activation is quantized per 32-block like ``quantize_int4``
@@ -262,20 +286,7 @@ def w4a4_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None,
     this restatement is unpinned beyond its quantizer."""
     x = np.asarray(x, dtype=np.float32)
     pa, sa = quantize_pack_int4(x, block, div_mode="recip")
-    ca = unpack_int4_codes(pa).astype(np.int64)
-    cb = unpack_int4_codes(np.asarray(packed)).astype(np.int64)
-    M, K = ca.shape
-    N = cb.shape[0]
-    nb = K // block
-    dots = np.einsum("mbk,nbk->mnb", ca.reshape(M, nb, block), cb.reshape(N, nb, block))  # exact integers
-    sab = (sa.astype(np.float32)[:, None, :] * np.asarray(scale, np.float32)[None, :, :]).astype(np.float32)
-    acc = np.zeros((M, N), dtype=np.float32)
-    for b in range(nb):  # fmaf: exact product + sum in float64, one rounding to float32
-        acc = (dots[:, :, b].astype(np.float64) * sab[:, :, b].astype(np.float64) + acc.astype(np.float64)).astype(
-            np.float32)
-    if bias is not None:
-        acc = acc + np.asarray(bias, dtype=np.float32)
-    return acc
+    return block_int_matmul(unpack_int4_codes(pa), sa, unpack_int4_codes(np.asarray(packed)), scale, bias, block)
 
 
 def w8a16_matmul(x: np.ndarray, q: np.ndarray, s: np.ndarray, bias=None) -> np.ndarray:

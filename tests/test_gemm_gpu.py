@@ -283,6 +283,21 @@ def test_gemm_int8_cta_pair_matches_single_cta(cuda, monkeypatch, per_channel):
     torch.testing.assert_close(out["1"], out["2"], rtol=1e-5, atol=1e-5 * out["1"].abs().max().item())
 
 
+def test_gemm_config1_single_linear_full(cuda):
+    """Config 1 exactly: X [256, 3072] bf16 ~ N(0, 1), W [3072, 3072] from
+    synthetic Q4_0 blocks (u ~ U{0..15}, d = fp16(|N(0, 0.02)|/7 + 1e-4)),
+    no bias, bf16 output; every element checked against the fp32
+    dequant-then-matmul, and the fp32 output against the exact-operand oracle."""
+    M, N, K = 256, 3072, 3072
+    p, s, pd, sd = _weights(N, K, seed=101, dev=cuda)
+    xn, xd = _x(M, K, seed=102, dev=cuda)
+    y = ops.gemm_w4a16(xd, pd, sd, None, torch.bfloat16)
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    _check(y.float().cpu().numpy(), O.w4a16_matmul(xn, p, s))
+    y32 = ops.gemm_w4a16(xd, pd, sd, None, torch.float32).cpu().numpy()
+    _check(y32, O.w4a16_matmul_bf16w(xn, p, s), 1e-5, 1e-5)
+
+
 @pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
 def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
     """The Flux linear sweep (config 2) at full size. The oracle checks 96 sampled token rows

@@ -72,3 +72,43 @@ def test_linear_activation_quant_flag(cuda):
     y = lin(torch.from_numpy(x).to(cuda)).cpu().numpy()
     m = O.parity_metrics(y, O.w4a4_matmul(x, p, s))
     assert m["max_abs_over_max_ref"] <= 2e-2 and m["mean_rel"] <= 5e-3, m
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [2, 200])
+def test_gemm_int4_reference_op(cuda, M):
+    """ops.gemm_int4 with the reference's arguments (A from quantize_int4)."""
+    from comfy_ui_gfx906_tools_b200 import ops
+    N, K = 320, 768
+    x, p, s = _case(M, N, K, 20 + M)
+    A, As = ops.quantize_int4(torch.from_numpy(x).to(cuda))
+    bias = torch.linspace(-1, 1, N, device=cuda)
+    y = ops.gemm_int4(A, As, torch.from_numpy(p).to(cuda), torch.from_numpy(s).to(cuda), bias, torch.float32)
+    ref = O.block_int_matmul(O.unpack_int4_codes(A.cpu().numpy()), As.cpu().numpy(), O.unpack_int4_codes(p), s,
+                             bias.cpu().numpy())
+    m = O.parity_metrics(y.cpu().numpy(), ref)
+    assert m["max_abs_over_max_ref"] <= 2e-2 and m["mean_rel"] <= 5e-3, m
+    with pytest.raises(RuntimeError, match="qblock=16"):
+        ops.gemm_int4(A, As.reshape(-1).repeat_interleave(2), torch.from_numpy(p).to(cuda),
+                      torch.from_numpy(s).reshape(-1).repeat_interleave(2).to(cuda), None, torch.float32, qblock=16)
+    with pytest.raises(RuntimeError, match="scales must be"):
+        ops.gemm_int4(A, As[:, :1], torch.from_numpy(p).to(cuda), torch.from_numpy(s).to(cuda), None, torch.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [3, 300])
+def test_gemm_int8_reference_op(cuda, M):
+    """ops.gemm_int8 with the reference's arguments (A, B from quantize_int8)."""
+    from comfy_ui_gfx906_tools_b200 import ops
+    N, K = 256, 1024
+    rng = np.random.default_rng(30 + M)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(cuda)
+    w = torch.from_numpy((rng.standard_normal((N, K)) * 0.05).astype(np.float32)).to(cuda)
+    A, As = ops.quantize_int8(x)
+    B, Bs = ops.quantize_int8(w)
+    y = ops.gemm_int8(A, As, B, Bs, None, torch.float32, config=1)
+    ref = O.block_int_matmul(A.cpu().numpy(), As.cpu().numpy(), B.cpu().numpy(), Bs.cpu().numpy())
+    m = O.parity_metrics(y.cpu().numpy(), ref)
+    assert m["max_abs_over_max_ref"] <= 2e-2 and m["mean_rel"] <= 5e-3, m
+    with pytest.raises(RuntimeError, match="config must be"):
+        ops.gemm_int8(A, As, B, Bs, None, torch.float32, config=4)
