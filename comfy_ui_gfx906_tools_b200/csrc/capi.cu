@@ -126,7 +126,7 @@ int gfx_device_status(int clear) {
   int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return -set_error(GFX_ERR_CUDA, "gfx_device_status: %s", cudaGetErrorString(e));
-  const int parts[3] = {splitk_device_status(clear), tc_device_status(clear), selftest_device_status(clear)};
+  const int parts[3] = {smallm_device_status(clear), tc_device_status(clear), selftest_device_status(clear)};
   for (int p : parts) {
     if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
     if (p && !v) v = p;
@@ -137,13 +137,13 @@ int gfx_device_status(int clear) {
 size_t w4a16_workspace_bytes(int M, int N, int K, int splits) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 0;  // the tensor-core path needs no scratch
-  return splitk_workspace_bytes(M, N, K, splits, sm_count(current_device()));
+  return smallm_workspace_bytes(M, N, K, splits, sm_count(current_device()));
 }
 
 int w4a16_auto_splits(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 1;
   if (w4a16_tc_supported(M, N, K, GFX_SCALE_F32)) return 1;
-  return splitk_auto_splits(M, N, K, sm_count(current_device()));
+  return smallm_auto_splits(M, N, K, sm_count(current_device()));
 }
 
 int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype, const void* bias,
@@ -159,7 +159,7 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
   // reference where `splits` changes speed, not the result's definition).
   if (w4a16_tc_supported(M, N, K, scale_dtype))
     return launch_w4a16_tc(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, st, sms);
-  return launch_w4a16_splitk(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, workspace,
+  return launch_w4a16_smallm(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, workspace,
                              workspace_bytes, st, sms);
 }
 

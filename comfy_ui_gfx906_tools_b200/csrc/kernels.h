@@ -15,13 +15,13 @@ constexpr size_t kSplitKCounterBytes = 256 * 1024;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// W4A16, small M (split-K, mma.sync register dequant) -- w4a16_splitk.cu
-int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+// W4A16, small M (split-K / stream-K, mma.sync register dequant) -- w4a16_smallm.cu
+int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                         int out_dtype, int M, int N, int K, int splits, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream, int sms);
-size_t splitk_workspace_bytes(int M, int N, int K, int splits, int sms);
-int splitk_auto_splits(int M, int N, int K, int sms);
-int splitk_device_status(int clear);
+size_t smallm_workspace_bytes(int M, int N, int K, int splits, int sms);
+int smallm_auto_splits(int M, int N, int K, int sms);
+int smallm_device_status(int clear);
 
 // W4A16 / W8A16, large M (tcgen05 + TMEM, persistent) -- w4a16_tc.cu
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,

@@ -89,7 +89,7 @@ extern "C" int w4a16_gemm_noalloc(const void* x, int x_dtype, const void* w_q4, 
     return set_error(GFX_ERR_INVALID, "w4a16_gemm_noalloc: x and weights must be 16-byte, scales 4-byte aligned");
   const int dev = current_device();
   const int sms = sm_count(dev);
-  const size_t need = splitk_workspace_bytes(M, N, K, splits, sms);
+  const size_t need = smallm_workspace_bytes(M, N, K, splits, sms);
   if (need > kNoAllocScratchBytes)
     return set_error(GFX_ERR_UNSUPPORTED,
                      "w4a16_gemm_noalloc: M=%d N=%d K=%d needs %zu bytes of scratch, more than the fixed %zu; "
@@ -97,6 +97,6 @@ extern "C" int w4a16_gemm_noalloc(const void* x, int x_dtype, const void* w_q4, 
   void* scratch = nullptr;
   int rc = noalloc_scratch(dev, &scratch);
   if (rc) return rc;
-  return launch_w4a16_splitk(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, scratch,
+  return launch_w4a16_smallm(x, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, scratch,
                              kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream), sms);
 }

@@ -11,8 +11,11 @@
 //  * Work is a grid of units (128 weight rows x 256 K). CTA c of G takes the
 //    contiguous unit range [c*U/G, (c+1)*U/G) in row-block-major order
 //    ("stream-K"): every CTA streams the same number of weight bytes, so there
-//    is no partial last wave. An explicit split count S is the special case
-//    G = row_blocks * S (each row block cut into S equal K segments).
+//    is no partial last wave. A split count S is the special case
+//    G = row_blocks * S (each row block cut into S equal K segments); the host
+//    plan picks it whenever a divisor S of the row block's unit count fills at
+//    least 90% of the resident CTA slots (one segment end per CTA), and
+//    stream-K otherwise.
 //  * One producer warp streams each unit's nibbles (TMA, SWIZZLE_128B), group
 //    scales (TMA when the scale row stride is 16-byte aligned, else cp.async)
 //    and the matching 256-wide slice of the activations (TMA, SWIZZLE_128B
@@ -568,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 // ---------------------------------------------------------------------------
 // host launcher
 // ---------------------------------------------------------------------------
-GFX_DEFINE_STATUS_READER(splitk_device_status)
+GFX_DEFINE_STATUS_READER(smallm_device_status)
 
 struct SmallMPlan {
   int nt, tok, tok_blocks, RB, KS, G, max_segs, ctas_per_sm, stages;
@@ -621,7 +624,7 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
   return p;
 }
 
-size_t splitk_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
+size_t smallm_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   // sized for the larger of the fp16 / fp32 scale plans
   size_t need = 0;
@@ -634,7 +637,7 @@ size_t splitk_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
   return need;
 }
 
-int splitk_auto_splits(int M, int N, int K, int sms) {
+int smallm_auto_splits(int M, int N, int K, int sms) {
   SmallMPlan p = smallm_plan(M, N, K, 0, sms, true);
   return (p.G + p.RB - 1) / p.RB;
 }
@@ -746,7 +749,7 @@ static int launch_smallm_out(int out_dtype, const SmallMPlan& p, const SmallMArg
   return launch_smallm_t<NT, STAGES, F16S, __nv_bfloat16>(p, a, st);
 }
 
-int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
+int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                         int out_dtype, int M, int N, int K, int splits_req, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream, int sms) {
   const bool f16 = scale_dtype == GFX_SCALE_F16;
@@ -755,7 +758,7 @@ int launch_w4a16_splitk(const void* x, const void* wq, const void* ws, int scale
                      "use splits=0 so larger M runs on the tensor-core kernel", M);
   SmallMPlan p = smallm_plan(M, N, K, splits_req, sms, f16);
   SmallMArgs a{};
-  const size_t need = splitk_workspace_bytes(M, N, K, splits_req, sms);
+  const size_t need = smallm_workspace_bytes(M, N, K, splits_req, sms);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(GFX_ERR_WORKSPACE, "w4a16_gemm: workspace of %zu bytes required, got %zu (ptr %p)", need,
                      workspace_bytes, workspace);
