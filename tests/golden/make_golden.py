@@ -123,7 +123,7 @@ def main():
         deq = dequant_train(packed, scale, 32)
         out[f"qp_{name}_dequant_f32"] = deq.numpy()
 
-    # --- Q4_0 ingest: synthetic ggml blocks (BASELINE generators), repacked by the reference ---
+    # --- Q4_0 ingest: synthetic ggml blocks (the benchmark generators), repacked by the reference ---
     N, K = 40, 192
     u = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32)
     d = (torch.randn(N, K // 32, generator=g).abs() * 0.02 / 7 + 1e-4).half()

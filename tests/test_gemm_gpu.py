@@ -342,7 +342,7 @@ def test_gemm_int8_block_scales(cuda, M, N, K):
 
 @pytest.mark.parametrize("M", [64, 4608])
 def test_gemm_int8_channel_scales_flux(cuda, M):
-    # int8 ~round(N(0,40)) clipped, one fp16 scale per output channel
+    # config 3: int8 ~round(N(0,40)) clipped, one fp16 scale per output channel
     K, N = 3072, 3072
     q, s = synthetic.int8_weight(N, K, seed=5)
     x = synthetic.activations(M, K, seed=6)
