@@ -169,3 +169,27 @@ class ChannelShardLinear(torch.nn.Module):
         dist.all_gather_into_tensor(full, y2, group=self.group)  # rank-major blocks of rows
         full = full.view(self.world, y2.shape[0], n_local).permute(1, 0, 2).reshape(y2.shape[0], -1)
         return full.reshape(*lead, self.world * n_local)
+
+
+def token_shard_linear(linear, x: torch.Tensor, group=None, gather: bool = True, local_forward=None) -> torch.Tensor:
+    """Token-row split of one large-M linear (weights replicated on every
+    rank): rank r computes rows [r*M/G, (r+1)*M/G) of x [..., M, K] -> y, and
+    one ``all_gather_into_tensor`` rebuilds y [..., M, N] on every rank when
+    ``gather`` (else the rank's rows are returned). No exchange is needed for
+    the GEMM itself. ``local_forward(linear, x)`` computes the local rows; it
+    defaults to ``linear(x)`` (the CUDA kernels)."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    lead, K = x.shape[:-1], x.shape[-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if M % world != 0:
+        raise ValueError(f"token rows ({M}) must divide evenly over {world} ranks for the token split")
+    per = M // world
+    _log_plan("tokens", world=world, rank=rank, rows=f"{rank * per}:{(rank + 1) * per}", M=M)
+    xs = x2[rank * per:(rank + 1) * per]
+    y = local_forward(linear, xs) if local_forward is not None else linear(xs)
+    if not gather:
+        return y
+    full = torch.empty(world * per, y.shape[-1], dtype=y.dtype, device=y.device)
+    dist.all_gather_into_tensor(full, y.contiguous(), group=group)  # rank-major = row order
+    return full.reshape(*lead, y.shape[-1])

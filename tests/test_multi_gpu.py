@@ -1,5 +1,5 @@
 """Splits across two GPUs over NCCL (skipped with fewer than two GPUs): the
-output-channel split of an int4 linear and the batch / token-row splits of an
+output-channel and token-row splits of an int4 linear and the batch / token-row splits of an
 int4 DiT match the same computation on one GPU. Every rank runs as its own
 spawned process with a short process-group timeout."""
 import datetime
@@ -46,6 +46,11 @@ def _worker(rank, world, port, q):
             ref = lin(x).float()
             got = split(x).float()
             out[f"channel_m{m}"] = float((got - ref).abs().max() / ref.abs().max())
+        # token-row split of the same linear at large M (weights replicated)
+        xt = synthetic.activations(512, K, seed=5).to(dev)
+        ref = lin(xt).float()
+        got = parallel.token_shard_linear(lin, xt).float()
+        out["tokens"] = float((got - ref).abs().max() / ref.abs().max())
         # int4 DiT (tiny): batch split and token-row split against the one-GPU forward
         cfg = flux_dit.tiny_config(depth_double=2, depth_single=2)
         model = flux_dit.FluxDiT(cfg, flux_dit.int4_linear_factory(dev, seed=11), dev)
@@ -80,5 +85,6 @@ def test_two_gpu_splits_match_one_gpu():
         assert status == "ok", val
         # the channel split reorders nothing inside a dot product: fp32 rounding only
         assert val["channel_m1"] < 1e-2 and val["channel_m16"] < 1e-2, val
+        assert val["tokens"] < 1e-6, val  # the same rows through the same kernel
         # bf16 activations through 4 blocks; the split changes only which GPU computes what
         assert val["batch"] < 2e-2 and val["rows"] < 2e-2, val

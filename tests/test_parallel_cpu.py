@@ -108,7 +108,13 @@ def _channel_split_error(parallel):
     assert got.shape == ref.shape == (1, M, N)
     local = split(x, gather=False)
     assert local.shape == (1, M, N // 2)
-    return float((got - ref).abs().max() / ref.abs().max())
+    # token-row split of the same layer (large-M case): rows [r*M/G, (r+1)*M/G) per rank
+    xt = torch.randn(2, 4, K, generator=g)
+    got_t = parallel.token_shard_linear(lin, xt, local_forward=oracle_forward)
+    ref_t = oracle_forward(lin, xt)
+    assert got_t.shape == ref_t.shape == (2, 4, N)
+    err_t = float((got_t - ref_t).abs().max() / ref_t.abs().max())
+    return max(float((got - ref).abs().max() / ref.abs().max()), err_t)
 
 
 def _run(mode):
