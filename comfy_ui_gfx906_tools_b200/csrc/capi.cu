@@ -163,6 +163,41 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
                              workspace_bytes, st, sms);
 }
 
+int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+                         const void* bias, void* const* y_ranks, int n_ranks, int rank, int out_dtype, int M,
+                         int N_local, int K, int splits, void* workspace, size_t workspace_bytes,
+                         gfx_stream_t stream) {
+  if (n_ranks < 1 || n_ranks > gfx::kMaxOutTargets || rank < 0 || rank >= n_ranks || !y_ranks)
+    return set_error(GFX_ERR_INVALID, "w4a16_gemm_allgather: need 1 <= n_ranks <= %d, 0 <= rank < n_ranks and the "
+                     "ranks' output pointers (got n_ranks=%d rank=%d)", gfx::kMaxOutTargets, n_ranks, rank);
+  for (int q = 0; q < n_ranks; ++q)
+    if (!y_ranks[q]) return set_error(GFX_ERR_INVALID, "w4a16_gemm_allgather: output pointer of rank %d is null", q);
+  int rc = check_gemm_common("w4a16_gemm_allgather", x, x_dtype, w_q4, w_scale, scale_dtype, y_ranks[0], out_dtype,
+                             M, N_local, K, splits);
+  if (rc) return rc;
+  if (M > 64)
+    return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm_allgather: M <= 64 only (the HBM-bound case), got M=%d", M);
+  if (M == 0) return GFX_OK;
+  gfx::OutTargets t{};
+  for (int q = 0; q < n_ranks; ++q) t.ptr[q] = y_ranks[q];
+  t.count = n_ranks;
+  t.ldy = N_local * n_ranks;
+  t.col0 = rank * N_local;
+  t.fence_sys = 1;
+  return launch_w4a16_smallm_targets(x, w_q4, w_scale, scale_dtype, bias, t, out_dtype, M, N_local, K, splits,
+                                     workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
+                                     sm_count(current_device()));
+}
+
+int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, int epoch, gfx_stream_t stream) {
+  if (n_ranks < 1 || n_ranks > gfx::kMaxOutTargets || rank < 0 || rank >= n_ranks || !flags_ranks)
+    return set_error(GFX_ERR_INVALID, "gfx_peer_barrier: need 1 <= n_ranks <= %d and 0 <= rank < n_ranks",
+                     gfx::kMaxOutTargets);
+  for (int q = 0; q < n_ranks; ++q)
+    if (!flags_ranks[q]) return set_error(GFX_ERR_INVALID, "gfx_peer_barrier: flag pointer of rank %d is null", q);
+  return gfx::launch_peer_barrier(flags_ranks, n_ranks, rank, epoch, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,
                const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
                size_t workspace_bytes, gfx_stream_t stream) {

@@ -47,6 +47,7 @@ enum DeviceErrorCode : int {
   kDevErrEpilogueBarrierTimeout = 4,
   kDevErrClusterReduceTimeout = 5,
   kDevErrSelfTestTimeout = 6,  // gfx_selftest_wait_timeout: the expected outcome
+  kDevErrPeerBarrierTimeout = 7,
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {

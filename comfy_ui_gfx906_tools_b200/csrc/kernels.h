@@ -15,10 +15,28 @@ constexpr size_t kSplitKCounterBytes = 256 * 1024;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Where the small-M kernel stores y: `count` copies (one per target buffer, for
+// example every rank's copy of a symmetric-memory buffer reached over NVLink),
+// each [M, ldy] with this launch's N columns starting at column col0. With
+// fence_sys set, every storing thread ends with a system-scope fence so that a
+// following cross-GPU barrier publishes the peer stores.
+constexpr int kMaxOutTargets = 8;
+struct OutTargets {
+  void* ptr[kMaxOutTargets];
+  int count;
+  int ldy;
+  int col0;
+  int fence_sys;
+};
+
 // W4A16, small M (split-K / stream-K, mma.sync register dequant) -- w4a16_smallm.cu
 int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                         int out_dtype, int M, int N, int K, int splits, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream, int sms);
+int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias,
+                                const OutTargets& out, int out_dtype, int M, int N, int K, int splits,
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream, int sms);
+int launch_peer_barrier(int* const* flags, int n_ranks, int rank, int epoch, cudaStream_t stream);
 size_t smallm_workspace_bytes(int M, int N, int K, int splits, int sms);
 int smallm_auto_splits(int M, int N, int K, int sms);
 int smallm_device_status(int clear);

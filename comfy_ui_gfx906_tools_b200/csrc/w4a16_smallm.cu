@@ -137,6 +137,14 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumerWarps * 32) : "memory");
 }
 
+// One output element to every target (the local y, or every rank's y).
+template <typename OutT>
+__device__ __forceinline__ void store_out(const OutTargets& out, int tok, int n, float v) {
+  const OutT val = from_f32<OutT>(v);
+  const size_t off = (size_t)tok * out.ldy + out.col0 + n;
+  for (int q = 0; q < out.count; ++q) reinterpret_cast<OutT*>(out.ptr[q])[off] = val;
+}
+
 // Token row of MMA column n within an 8-token tile (conflict-free activation loads).
 __device__ __forceinline__ int tok_perm(int n) { return (n >> 1) | ((n & 1) << 2); }
 
@@ -150,7 +158,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
-    const OutT* __restrict__ bias, OutT* __restrict__ y, float* __restrict__ partials, int* __restrict__ counters,
+    const OutT* __restrict__ bias, const __grid_constant__ OutTargets out, float* __restrict__ partials,
+    int* __restrict__ counters,
     int M, int N, int K, int G, int max_segs) {
   using L = Layout<NT, STAGES, kF16Scale>;
   constexpr int kTok = L::kTok;
@@ -430,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
               for (int cc = 0; cc < 2; ++cc) {
                 const int tok = tok0 + nt * 8 + tok_perm(2 * t_ + cc);
-                if (tok < M) y[(size_t)tok * N + n] = from_f32<OutT>(acc[mt][nt][half * 2 + cc] + bv);
+                if (tok < M) store_out<OutT>(out, tok, n, acc[mt][nt][half * 2 + cc] + bv);
               }
           }
       }
@@ -482,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
                   if (tok >= vt) continue;
                   float v = acc[mt][nt][half * 2 + cc];
                   for (uint32_t q = 1; q < csize; ++q) v += recv[((q - 1) * kTok + tok) * kRecvStride + r];
-                  y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(v + bv);
+                  store_out<OutT>(out, tok0 + tok, n, v + bv);
                 }
             }
         }
@@ -547,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
             if (n >= N) continue;
             float o = vv[e];
             if (bias) o += to_f32(bias[n]);
-            y[(size_t)(tok0 + tok) * N + n] = from_f32<OutT>(o);
+            store_out<OutT>(out, tok0 + tok, n, o);
           }
         }
         if (tc == 0) *counter = 0;
@@ -563,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
   }
+  if (out.fence_sys) __threadfence_system();  // publish peer-buffer stores before a cross-GPU barrier
   if constexpr (kCl) cluster_sync_all();  // no CTA of the cluster leaves while a peer may address it
 }
 
@@ -647,7 +657,7 @@ struct SmallMArgs {
   int scale_tma;
   const void* ws;
   const void* bias;
-  void* y;
+  OutTargets out;
   float* part;
   int* cnt;
   int M, N, K;
@@ -675,7 +685,7 @@ static int launch_smallm_k(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
     cfg.numAttrs = 2;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
-                                     (const OutT*)a.bias, (OutT*)a.y, a.part, a.cnt, a.M, a.N, a.K, p.G, p.max_segs);
+                                     (const OutT*)a.bias, a.out, a.part, a.cnt, a.M, a.N, a.K, p.G, p.max_segs);
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a16_smallm_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a16_smallm_kernel");
 }
@@ -752,6 +762,19 @@ static int launch_smallm_out(int out_dtype, const SmallMPlan& p, const SmallMArg
 int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                         int out_dtype, int M, int N, int K, int splits_req, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream, int sms) {
+  OutTargets out{};
+  out.ptr[0] = y;
+  out.count = 1;
+  out.ldy = N;
+  out.col0 = 0;
+  out.fence_sys = 0;
+  return launch_w4a16_smallm_targets(x, wq, ws, scale_dtype, bias, out, out_dtype, M, N, K, splits_req, workspace,
+                                     workspace_bytes, stream, sms);
+}
+
+int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias,
+                                const OutTargets& out, int out_dtype, int M, int N, int K, int splits_req,
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream, int sms) {
   const bool f16 = scale_dtype == GFX_SCALE_F16;
   if (M > 64)
     return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm: the small-M kernel takes M <= 64 (got M=%d); "
@@ -789,7 +812,7 @@ int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale
   }
   a.ws = ws;
   a.bias = bias;
-  a.y = y;
+  a.out = out;
   a.M = M;
   a.N = N;
   a.K = K;
@@ -802,6 +825,44 @@ int launch_w4a16_smallm(const void* x, const void* wq, const void* ws, int scale
   if (p.nt == 1) return launch_smallm_out<1, 4, false>(out_dtype, p, a, stream);
   if (p.nt == 2) return launch_smallm_out<2, 3, false>(out_dtype, p, a, stream);
   return launch_smallm_out<4, 6, false>(out_dtype, p, a, stream);
+}
+
+// ---------------------------------------------------------------------------
+// cross-GPU flag barrier for the all-gather epilogue
+// ---------------------------------------------------------------------------
+// flags[q] is rank q's array of n_ranks ints (symmetric memory, reachable from
+// every rank). Thread q of rank r stores `epoch` into flags[q][r] with release
+// at system scope, then waits -- bounded -- until flags[r][q] >= epoch with
+// acquire at system scope: after it, every store rank q made before its own
+// release (its GEMM's writes into this rank's y) is visible here. Epochs grow
+// by one per call, so the flags never need re-arming.
+struct FlagTable {
+  int* p[kMaxOutTargets];
+};
+
+__global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int n_ranks, int rank, int epoch) {
+  const int q = threadIdx.x;
+  if (q >= n_ranks) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(flags.p[q] + rank), "r"(epoch) : "memory");
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags.p[rank] + q) : "memory");
+    if (v - epoch >= 0) break;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      record_device_error(kDevErrPeerBarrierTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
+int launch_peer_barrier(int* const* flags, int n_ranks, int rank, int epoch, cudaStream_t stream) {
+  FlagTable t{};
+  for (int q = 0; q < n_ranks; ++q) t.p[q] = flags[q];
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(t, n_ranks, rank, epoch);
+  return check_launch("peer_barrier_kernel");
 }
 
 }  // namespace gfx

@@ -135,9 +135,18 @@ class ChannelShardLinear(torch.nn.Module):
 
     ``local_forward(shard, x)`` computes the local slice; it defaults to the
     shard module's own forward (the CUDA kernels).
+
+    ``fused=True`` (CUDA, M <= 64, weight-only mode) replaces the GEMM + NCCL
+    all-gather by ONE kernel whose epilogue stores the rank's columns straight
+    into every rank's copy of a symmetric-memory y buffer over NVLink
+    (``w4a16_gemm_allgather``), followed by a bounded flag barrier over the
+    same memory (``gfx_peer_barrier``). Two y buffers alternate between calls,
+    so a peer never overwrites a buffer another rank may still be reading.
     """
 
-    def __init__(self, linear, group=None, local_forward=None):
+    _Y_ROWS = 64  # rows of the symmetric y buffers (the small-M kernel's limit)
+
+    def __init__(self, linear, group=None, local_forward=None, fused: bool = False):
         super().__init__()
         from .ops import Gfx906Int4Ops
         if not getattr(linear, "quantized", False):
@@ -158,8 +167,65 @@ class ChannelShardLinear(torch.nn.Module):
                 shard.bias.copy_(linear.bias[n0:n1])
         self.shard = shard
         self.local_forward = local_forward
+        self.fused = fused
+        self._sym = None
+        self._epoch = 0
+
+    def _symmetric(self, dtype, device):
+        """Two [64, N] y buffers and the barrier flags in symmetric memory,
+        mapped on every rank (allocated once per dtype)."""
+        key = (dtype, device)
+        if self._sym is None or self._sym[0] != key:
+            import torch.distributed._symmetric_memory as symm_mem
+            group_name = (self.group or dist.group.WORLD).group_name
+            ybuf = symm_mem.empty((2, self._Y_ROWS, self.out_features), dtype=dtype, device=device)
+            yh = symm_mem.rendezvous(ybuf, group_name)
+            flags = symm_mem.empty((self.world,), dtype=torch.int32, device=device)
+            flags.zero_()
+            fh = symm_mem.rendezvous(flags, group_name)
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.group)  # every rank's flags are zero before the first barrier
+            self._sym = (key, ybuf, list(yh.buffer_ptrs), flags, list(fh.buffer_ptrs))
+            self._epoch = 0
+        return self._sym
+
+    def _forward_fused(self, x: torch.Tensor) -> torch.Tensor:
+        import ctypes
+
+        from . import _lib, ops
+        sh = self.shard
+        lead, K = x.shape[:-1], x.shape[-1]
+        x2 = x.reshape(-1, K)
+        if sh.rotation_group:
+            x2 = ops.hadamard_rotate(x2, sh.rotation_group, torch.bfloat16)
+        xb = x2.to(torch.bfloat16).contiguous()
+        M, n_local = xb.shape[0], sh.out_features
+        _, ybuf, y_ptrs, _, f_ptrs = self._symmetric(x.dtype, x.device)
+        scale = sh._device_scale(sh.weight_scale)
+        bias = sh.bias.to(x.dtype).contiguous() if sh.bias is not None else None
+        parity = self._epoch & 1
+        self._epoch += 1
+        row_bytes = self.out_features * ybuf.element_size()
+        targets = (ctypes.c_void_p * self.world)(*[p + parity * self._Y_ROWS * row_bytes for p in y_ptrs])
+        flags = (ctypes.c_void_p * self.world)(*f_ptrs)
+        with torch.cuda.device(x.device):
+            stream = torch.cuda.current_stream(x.device).cuda_stream
+            L = _lib.load()
+            ws = ops._workspace(x.device, stream, int(L.w4a16_workspace_bytes(M, n_local, K, 0)))
+            _lib.call("w4a16_gemm_allgather", xb.data_ptr(), _lib.DTYPE_BF16, sh.weight_q4.data_ptr(), scale.data_ptr(),
+                      _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32,
+                      bias.data_ptr() if bias is not None else None, ctypes.cast(targets, ctypes.c_void_p), self.world,
+                      self.rank, ops._dtype_code(x.dtype), M, n_local, K, 0,
+                      ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
+            _lib.call("gfx_peer_barrier", ctypes.cast(flags, ctypes.c_void_p), self.world, self.rank, self._epoch,
+                      stream)
+        return ybuf[parity, :M].clone().reshape(*lead, self.out_features)
 
     def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        rows = x.numel() // x.shape[-1]
+        if (self.fused and gather and self.local_forward is None and x.is_cuda and rows <= self._Y_ROWS
+                and not getattr(self.shard, "activation_quant", False)):
+            return self._forward_fused(x)
         y = self.local_forward(self.shard, x) if self.local_forward is not None else self.shard(x)
         if not gather:
             return y

@@ -58,6 +58,30 @@ int gfx_version(void);
  * resets the word to 0. */
 int gfx_device_status(int clear);
 
+/* Output-channel split of one W4A16 GEMM with the all-gather fused into its
+ * epilogue (no reference counterpart: the reference splits tokens or the batch
+ * across two GPUs, row_split.py:122-241; this is the B200 form of an
+ * output-channel split for M <= 64). This rank computes y[:, rank*N_local :
+ * (rank+1)*N_local] from its shard w_q4 [N_local, K/2] / w_scale and bias
+ * [N_local] (or NULL), and stores it into EVERY rank's y buffer
+ * (y_ranks[q]: rank q's [M, n_ranks*N_local] buffer, mapped on this device,
+ * e.g. symmetric memory reached over NVLink) with plain stores and a
+ * system-scope fence. Follow it with gfx_peer_barrier before reading y; a
+ * buffer must not be rewritten while a peer may still read it (alternate two
+ * buffers). 1 <= n_ranks <= 8, M <= 64; other arguments as w4a16_gemm. */
+int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+                         const void* bias, void* const* y_ranks, int n_ranks, int rank, int out_dtype, int M,
+                         int N_local, int K, int splits, void* workspace, size_t workspace_bytes,
+                         gfx_stream_t stream);
+
+/* Cross-GPU barrier over NVLink-mapped flags (no reference counterpart):
+ * flags_ranks[q] is rank q's int[n_ranks] (zero before the first call). This
+ * rank stores `epoch` into flags_ranks[q][rank] for every q (release, system
+ * scope) and waits until flags_ranks[rank][q] >= epoch for every q (acquire,
+ * system scope); every rank passes the same epoch, one more per call. A wait
+ * that exceeds 2 s records status 7 (gfx_device_status) and returns. */
+int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, int epoch, gfx_stream_t stream);
+
 /* Failure-detection check (no reference counterpart; used by the tests): one
  * CTA waits on an mbarrier nothing arrives on, gives up after timeout_us
  * (0 < timeout_us <= 1e6) and records status code 6 in the device status

@@ -103,3 +103,20 @@ def test_hadamard_rotate_argument_checks(built_lib):
     assert b"group" in built_lib.gfx_last_error()
     assert built_lib.hadamard_rotate(None, 0, None, None, 0, 4, 96, 64, None) == 1
     assert built_lib.hadamard_rotate(None, 0, None, None, 0, 0, 128, 64, None) == 0  # rows == 0: no-op
+
+
+def test_allgather_and_peer_barrier_argument_checks(built_lib):
+    # argument checks only: nothing is launched
+    ptrs = (ctypes.c_void_p * 2)(16, 32)
+    nulls = (ctypes.c_void_p * 2)(16, None)
+    def ag(targets, n_ranks, rank, M=4):
+        return built_lib.w4a16_gemm_allgather(16, 2, 16, 16, 0, None, ctypes.cast(targets, ctypes.c_void_p), n_ranks,
+                                              rank, 2, M, 8, 64, 0, None, 0, None)
+    assert ag(ptrs, 9, 0) == _lib.GFX_ERR_INVALID and "n_ranks" in _lib.last_error()
+    assert ag(ptrs, 2, 2) == _lib.GFX_ERR_INVALID
+    assert ag(nulls, 2, 0) == _lib.GFX_ERR_INVALID and "rank 1 is null" in _lib.last_error()
+    assert ag(ptrs, 2, 1, M=65) == _lib.GFX_ERR_UNSUPPORTED and "M <= 64" in _lib.last_error()
+    assert ag(ptrs, 2, 1, M=0) == _lib.GFX_OK  # M == 0: no launch
+    assert built_lib.gfx_peer_barrier(ctypes.cast(ptrs, ctypes.c_void_p), 2, -1, 1, None) == _lib.GFX_ERR_INVALID
+    assert built_lib.gfx_peer_barrier(ctypes.cast(nulls, ctypes.c_void_p), 2, 0, 1, None) == _lib.GFX_ERR_INVALID
+    assert "rank 1 is null" in _lib.last_error()

@@ -1,5 +1,6 @@
 """Splits across two GPUs over NCCL (skipped with fewer than two GPUs): the
-output-channel and token-row splits of an int4 linear and the batch / token-row splits of an
+output-channel split (NCCL all-gather, and the fused kernel that stores into every rank's
+symmetric-memory buffer), the token-row split of an int4 linear and the batch / token-row splits of an
 int4 DiT match the same computation on one GPU. Every rank runs as its own
 spawned process with a short process-group timeout."""
 import datetime
@@ -46,6 +47,19 @@ def _worker(rank, world, port, q):
             ref = lin(x).float()
             got = split(x).float()
             out[f"channel_m{m}"] = float((got - ref).abs().max() / ref.abs().max())
+        # fused GEMV + all-gather over symmetric memory: six back-to-back calls (both y buffers used
+        # three times) must equal the NCCL split bit for bit, and no peer barrier may time out
+        from comfy_ui_gfx906_tools_b200 import _lib
+        _lib.load().gfx_device_status(1)
+        fused = parallel.ChannelShardLinear(lin, fused=True)
+        xs = [synthetic.activations(m, K, seed=20 + i).to(dev) for i, m in enumerate((1, 16, 64, 3, 1, 40))]
+        got = [fused(x) for x in xs]
+        torch.cuda.synchronize()
+        want = [split(x) for x in xs]
+        out["fused_exact"] = all(torch.equal(a, b) for a, b in zip(got, want))
+        out["fused_status"] = int(_lib.load().gfx_device_status(1))
+        out["fused_vs_one"] = max(float((g.float() - lin(x).float()).abs().max() / lin(x).float().abs().max())
+                                  for g, x in zip(got, xs))
         # token-row split of the same linear at large M (weights replicated)
         xt = synthetic.activations(512, K, seed=5).to(dev)
         ref = lin(xt).float()
@@ -85,6 +99,7 @@ def test_two_gpu_splits_match_one_gpu():
         assert status == "ok", val
         # the channel split reorders nothing inside a dot product: fp32 rounding only
         assert val["channel_m1"] < 1e-2 and val["channel_m16"] < 1e-2, val
+        assert val["fused_exact"] and val["fused_status"] == 0 and val["fused_vs_one"] < 1e-2, val
         assert val["tokens"] < 1e-6, val  # the same rows through the same kernel
         # bf16 activations through 4 blocks; the split changes only which GPU computes what
         assert val["batch"] < 2e-2 and val["rows"] < 2e-2, val
