@@ -313,9 +313,12 @@ def run_ours(args, world, rank, local):
                 sh.append((K, N, p[n0:n1].contiguous(), s[n0:n1].contiguous()))
             shard_sets.append(sh)
             del cp
-        tp = {"copies": ncopy, "split": f"output channels / {world}, all_gather_into_tensor of y"}
+        tp = {"copies": ncopy, "split": f"output channels / {world}, all_gather_into_tensor of y",
+              "fused": "w4a16_gemm_allgather (epilogue stores into every rank's symmetric-memory y) + peer barrier"}
+        sag = parallel.SymmetricAllGather(max(N for (_, _, N) in SHAPES), torch.bfloat16, dev)
         for Ms in (1, 16):
-            xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev) for i, (_, K, _) in enumerate(SHAPES)]
+            xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev).to(torch.bfloat16).contiguous()
+                   for i, (_, K, _) in enumerate(SHAPES)]
             outs = [torch.empty(world * Ms, N // world, dtype=torch.bfloat16, device=dev) for (_, _, N) in SHAPES]
 
             def tp_pass():
@@ -323,12 +326,29 @@ def run_ours(args, world, rank, local):
                     for (K, N, p, s), x, o in zip(sh, xsm, outs):
                         y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
                         dist.all_gather_into_tensor(o, y)
+
+            def fused_pass():
+                for sh in shard_sets:
+                    for (K, N, p, s), x in zip(sh, xsm):
+                        sag.gemm(x, p, s, None, N // world)
             reps = 5
-            ms = max_over_ranks(time_steps(tp_pass, reps, 2, world, dev, stream) / reps, world, dev)
             nbytes = ncopy * sum(N * K // 2 + N * (K // 32) * 2 + Ms * K * 2 + Ms * N * 2 for (_, K, N) in SHAPES)
-            tp[f"M{Ms}"] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (ncopy * len(SHAPES)),
-                            "frac_hbm_aggregate": (nbytes / (ms * 1e-3) / 1e9) / (world * pk["hbm_gbs"])}
-        del shard_sets
+            # the fused pass captured once in a CUDA graph (an even number of calls, so the
+            # y buffers keep alternating between replays): the host launches one graph
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fused_pass()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                fused_pass()
+            for key, fn in ((f"M{Ms}", tp_pass), (f"M{Ms}_fused", fused_pass), (f"M{Ms}_fused_graph", graph.replay)):
+                ms = max_over_ranks(time_steps(fn, reps, 2, world, dev, stream) / reps, world, dev)
+                tp[key] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (ncopy * len(SHAPES)),
+                           "frac_hbm_aggregate": (nbytes / (ms * 1e-3) / 1e9) / (world * pk["hbm_gbs"])}
+            del graph
+        del shard_sets, sag
 
     # --- int8 weights (config 3): the six shapes at M=4608, per-channel fp16 scales ---
     int8 = None

@@ -189,13 +189,13 @@ int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const voi
                                      sm_count(current_device()));
 }
 
-int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, int epoch, gfx_stream_t stream) {
+int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, gfx_stream_t stream) {
   if (n_ranks < 1 || n_ranks > gfx::kMaxOutTargets || rank < 0 || rank >= n_ranks || !flags_ranks)
     return set_error(GFX_ERR_INVALID, "gfx_peer_barrier: need 1 <= n_ranks <= %d and 0 <= rank < n_ranks",
                      gfx::kMaxOutTargets);
   for (int q = 0; q < n_ranks; ++q)
     if (!flags_ranks[q]) return set_error(GFX_ERR_INVALID, "gfx_peer_barrier: flag pointer of rank %d is null", q);
-  return gfx::launch_peer_barrier(flags_ranks, n_ranks, rank, epoch, reinterpret_cast<cudaStream_t>(stream));
+  return gfx::launch_peer_barrier(flags_ranks, n_ranks, rank, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale, int scale_per_channel,

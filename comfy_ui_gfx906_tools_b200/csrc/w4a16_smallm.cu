@@ -830,38 +830,47 @@ int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, i
 // ---------------------------------------------------------------------------
 // cross-GPU flag barrier for the all-gather epilogue
 // ---------------------------------------------------------------------------
-// flags[q] is rank q's array of n_ranks ints (symmetric memory, reachable from
-// every rank). Thread q of rank r stores `epoch` into flags[q][r] with release
-// at system scope, then waits -- bounded -- until flags[r][q] >= epoch with
-// acquire at system scope: after it, every store rank q made before its own
-// release (its GEMM's writes into this rank's y) is visible here. Epochs grow
-// by one per call, so the flags never need re-arming.
+// flags[q] is rank q's array of n_ranks + 1 ints (symmetric memory, reachable
+// from every rank); slot n_ranks of a rank's own array counts the barriers it
+// passed, so the epoch needs no host argument (graph-capturable). With e = that
+// count + 1, lane q of rank r stores e into flags[q][r] with release at system
+// scope, then waits -- bounded -- until flags[r][q] >= e with acquire at system
+// scope: after it, every store rank q made before its own release (its GEMM's
+// writes into this rank's y) is visible here. Only peers write flags[r][0..n),
+// only rank r writes flags[r][n], and the next barrier on this stream reads the
+// counter after this kernel ends.
 struct FlagTable {
   int* p[kMaxOutTargets];
 };
 
-__global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int n_ranks, int rank, int epoch) {
+__global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int n_ranks, int rank) {
   const int q = threadIdx.x;
-  if (q >= n_ranks) return;
-  __threadfence_system();
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(flags.p[q] + rank), "r"(epoch) : "memory");
-  const unsigned long long t0 = global_timer_ns();
-  for (;;) {
-    int v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags.p[rank] + q) : "memory");
-    if (v - epoch >= 0) break;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-      record_device_error(kDevErrPeerBarrierTimeout);
-      break;
+  int* own = flags.p[rank];
+  const int epoch = own[n_ranks] + 1;
+  __syncwarp();
+  if (q < n_ranks) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(flags.p[q] + rank), "r"(epoch) : "memory");
+    const unsigned long long t0 = global_timer_ns();
+    for (;;) {
+      int v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
+      if (v - epoch >= 0) break;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        record_device_error(kDevErrPeerBarrierTimeout);
+        break;
+      }
+      __nanosleep(64);
     }
-    __nanosleep(64);
   }
+  __syncwarp();
+  if (q == 0) own[n_ranks] = epoch;
 }
 
-int launch_peer_barrier(int* const* flags, int n_ranks, int rank, int epoch, cudaStream_t stream) {
+int launch_peer_barrier(int* const* flags, int n_ranks, int rank, cudaStream_t stream) {
   FlagTable t{};
   for (int q = 0; q < n_ranks; ++q) t.p[q] = flags[q];
-  peer_barrier_kernel<<<1, 32, 0, stream>>>(t, n_ranks, rank, epoch);
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(t, n_ranks, rank);
   return check_launch("peer_barrier_kernel");
 }
 

@@ -121,6 +121,71 @@ def channel_block(n: int, rank: int, world: int):
     return rank * per, (rank + 1) * per
 
 
+class SymmetricAllGather:
+    """y buffers and barrier flags in symmetric memory for the fused small-M
+    GEMM + all-gather (``w4a16_gemm_allgather`` then ``gfx_peer_barrier``).
+
+    Every rank maps every other rank's buffers (``torch.distributed``'s
+    symmetric memory over NVLink). One call's kernel stores the rank's
+    [M, N_local] block straight into columns [rank*N_local, (rank+1)*N_local)
+    of every rank's y; the flag barrier then makes the whole [M, N] visible.
+    Two y buffers alternate between calls: a rank writes buffer p again only
+    after the barrier of the call in between, which every peer reaches only
+    after it finished reading buffer p (its reads precede its next launch in
+    stream order), so no buffer is overwritten while a peer still reads it.
+    The barrier keeps its epoch on the device, so a sequence of calls can be
+    captured in a CUDA graph; capture an even number of calls, so that the
+    buffers keep alternating from one replay to the next.
+    """
+
+    ROWS = 64  # the small-M kernel's limit
+
+    def __init__(self, n_max: int, dtype: torch.dtype, device: torch.device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.n_max, self.dtype, self.device = n_max, dtype, device
+        group_name = (group or dist.group.WORLD).group_name
+        self.ybuf = symm_mem.empty((2, self.ROWS * n_max), dtype=dtype, device=device)
+        self.y_ptrs = list(symm_mem.rendezvous(self.ybuf, group_name).buffer_ptrs)
+        self.flags = symm_mem.empty((self.world + 1,), dtype=torch.int32, device=device)
+        self.flags.zero_()
+        self.f_ptrs = list(symm_mem.rendezvous(self.flags, group_name).buffer_ptrs)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before the first barrier
+        import ctypes
+        row = self.ROWS * n_max * self.ybuf.element_size()
+        # pointer arrays built once (they outlive every call that passes them)
+        self._target_arrs = [(ctypes.c_void_p * self.world)(*[p + k * row for p in self.y_ptrs]) for k in (0, 1)]
+        self._targets = [ctypes.cast(a, ctypes.c_void_p) for a in self._target_arrs]
+        self._flag_arr = (ctypes.c_void_p * self.world)(*self.f_ptrs)
+        self._flag_ptr = ctypes.cast(self._flag_arr, ctypes.c_void_p)
+        self.calls = 0
+
+    def gemm(self, xb: torch.Tensor, w_q4: torch.Tensor, scale: torch.Tensor, bias, n_local: int) -> torch.Tensor:
+        """y[M, world*n_local] (a view of the current buffer, valid until two
+        calls later) = the all-gather of every rank's xb @ dequant(w)^T (+ bias).
+        ``xb`` bf16 [M, K] contiguous, M <= 64; ``scale`` fp32 or fp16."""
+        from . import _lib, ops
+        M, K = xb.shape
+        n_total = n_local * self.world
+        if M > self.ROWS or n_total > self.n_max:
+            raise ValueError(f"fused all-gather takes M <= {self.ROWS}, N <= {self.n_max}; got M={M}, N={n_total}")
+        parity = self.calls & 1
+        self.calls += 1
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            L = _lib.load()
+            ws = ops._workspace(self.device, stream, int(L.w4a16_workspace_bytes(M, n_local, K, 0)))
+            _lib.call("w4a16_gemm_allgather", xb.data_ptr(), _lib.DTYPE_BF16, w_q4.data_ptr(), scale.data_ptr(),
+                      _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32,
+                      bias.data_ptr() if bias is not None else None, self._targets[parity], self.world,
+                      self.rank, ops._dtype_code(self.dtype), M, n_local, K, 0,
+                      ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
+            _lib.call("gfx_peer_barrier", self._flag_ptr, self.world, self.rank, stream)
+        return self.ybuf[parity, :M * n_total].view(M, n_total)
+
+
 class ChannelShardLinear(torch.nn.Module):
     """Output-channel split of one int4 linear for the M <= 16 (HBM-bound) case.
 
@@ -131,7 +196,7 @@ class ChannelShardLinear(torch.nn.Module):
     rebuilds y [M, N] on every rank, or y stays sharded (``gather=False``) for
     a following layer that consumes channel shards. The reference has no such
     split (its row_split.py splits tokens or the batch); this is the B200
-    re-design of §8(e)'s small-M case.
+    re-design for the small-M (HBM-bound) multi-GPU case.
 
     ``local_forward(shard, x)`` computes the local slice; it defaults to the
     shard module's own forward (the CUDA kernels).
@@ -140,11 +205,8 @@ class ChannelShardLinear(torch.nn.Module):
     all-gather by ONE kernel whose epilogue stores the rank's columns straight
     into every rank's copy of a symmetric-memory y buffer over NVLink
     (``w4a16_gemm_allgather``), followed by a bounded flag barrier over the
-    same memory (``gfx_peer_barrier``). Two y buffers alternate between calls,
-    so a peer never overwrites a buffer another rank may still be reading.
+    same memory (``gfx_peer_barrier``); see ``SymmetricAllGather``.
     """
-
-    _Y_ROWS = 64  # rows of the symmetric y buffers (the small-M kernel's limit)
 
     def __init__(self, linear, group=None, local_forward=None, fused: bool = False):
         super().__init__()
@@ -169,61 +231,24 @@ class ChannelShardLinear(torch.nn.Module):
         self.local_forward = local_forward
         self.fused = fused
         self._sym = None
-        self._epoch = 0
-
-    def _symmetric(self, dtype, device):
-        """Two [64, N] y buffers and the barrier flags in symmetric memory,
-        mapped on every rank (allocated once per dtype)."""
-        key = (dtype, device)
-        if self._sym is None or self._sym[0] != key:
-            import torch.distributed._symmetric_memory as symm_mem
-            group_name = (self.group or dist.group.WORLD).group_name
-            ybuf = symm_mem.empty((2, self._Y_ROWS, self.out_features), dtype=dtype, device=device)
-            yh = symm_mem.rendezvous(ybuf, group_name)
-            flags = symm_mem.empty((self.world,), dtype=torch.int32, device=device)
-            flags.zero_()
-            fh = symm_mem.rendezvous(flags, group_name)
-            torch.cuda.synchronize(device)
-            dist.barrier(group=self.group)  # every rank's flags are zero before the first barrier
-            self._sym = (key, ybuf, list(yh.buffer_ptrs), flags, list(fh.buffer_ptrs))
-            self._epoch = 0
-        return self._sym
 
     def _forward_fused(self, x: torch.Tensor) -> torch.Tensor:
-        import ctypes
-
-        from . import _lib, ops
+        from . import ops
         sh = self.shard
         lead, K = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, K)
         if sh.rotation_group:
             x2 = ops.hadamard_rotate(x2, sh.rotation_group, torch.bfloat16)
         xb = x2.to(torch.bfloat16).contiguous()
-        M, n_local = xb.shape[0], sh.out_features
-        _, ybuf, y_ptrs, _, f_ptrs = self._symmetric(x.dtype, x.device)
-        scale = sh._device_scale(sh.weight_scale)
+        if self._sym is None or self._sym.dtype != x.dtype or self._sym.device != x.device:
+            self._sym = SymmetricAllGather(self.out_features, x.dtype, x.device, self.group)
         bias = sh.bias.to(x.dtype).contiguous() if sh.bias is not None else None
-        parity = self._epoch & 1
-        self._epoch += 1
-        row_bytes = self.out_features * ybuf.element_size()
-        targets = (ctypes.c_void_p * self.world)(*[p + parity * self._Y_ROWS * row_bytes for p in y_ptrs])
-        flags = (ctypes.c_void_p * self.world)(*f_ptrs)
-        with torch.cuda.device(x.device):
-            stream = torch.cuda.current_stream(x.device).cuda_stream
-            L = _lib.load()
-            ws = ops._workspace(x.device, stream, int(L.w4a16_workspace_bytes(M, n_local, K, 0)))
-            _lib.call("w4a16_gemm_allgather", xb.data_ptr(), _lib.DTYPE_BF16, sh.weight_q4.data_ptr(), scale.data_ptr(),
-                      _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32,
-                      bias.data_ptr() if bias is not None else None, ctypes.cast(targets, ctypes.c_void_p), self.world,
-                      self.rank, ops._dtype_code(x.dtype), M, n_local, K, 0,
-                      ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
-            _lib.call("gfx_peer_barrier", ctypes.cast(flags, ctypes.c_void_p), self.world, self.rank, self._epoch,
-                      stream)
-        return ybuf[parity, :M].clone().reshape(*lead, self.out_features)
+        y = self._sym.gemm(xb, sh.weight_q4, sh._device_scale(sh.weight_scale), bias, sh.out_features)
+        return y.clone().reshape(*lead, self.out_features)
 
     def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
         rows = x.numel() // x.shape[-1]
-        if (self.fused and gather and self.local_forward is None and x.is_cuda and rows <= self._Y_ROWS
+        if (self.fused and gather and self.local_forward is None and x.is_cuda and rows <= SymmetricAllGather.ROWS
                 and not getattr(self.shard, "activation_quant", False)):
             return self._forward_fused(x)
         y = self.local_forward(self.shard, x) if self.local_forward is not None else self.shard(x)

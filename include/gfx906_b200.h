@@ -75,12 +75,15 @@ int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const voi
                          gfx_stream_t stream);
 
 /* Cross-GPU barrier over NVLink-mapped flags (no reference counterpart):
- * flags_ranks[q] is rank q's int[n_ranks] (zero before the first call). This
- * rank stores `epoch` into flags_ranks[q][rank] for every q (release, system
- * scope) and waits until flags_ranks[rank][q] >= epoch for every q (acquire,
- * system scope); every rank passes the same epoch, one more per call. A wait
- * that exceeds 2 s records status 7 (gfx_device_status) and returns. */
-int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, int epoch, gfx_stream_t stream);
+ * flags_ranks[q] is rank q's int[n_ranks + 1] (zero before the first call).
+ * The epoch lives on the device: slot n_ranks of this rank's own array counts
+ * the barriers it passed, so the call takes no per-call argument and can be
+ * captured in a CUDA graph. With e = that count + 1, this rank stores e into
+ * flags_ranks[q][rank] for every q (release, system scope), waits until
+ * flags_ranks[rank][q] >= e for every q (acquire, system scope) and stores e
+ * back into its counter. A wait that exceeds 2 s records status 7
+ * (gfx_device_status) and returns. */
+int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, gfx_stream_t stream);
 
 /* Failure-detection check (no reference counterpart; used by the tests): one
  * CTA waits on an mbarrier nothing arrives on, gives up after timeout_us

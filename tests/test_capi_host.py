@@ -117,6 +117,6 @@ def test_allgather_and_peer_barrier_argument_checks(built_lib):
     assert ag(nulls, 2, 0) == _lib.GFX_ERR_INVALID and "rank 1 is null" in _lib.last_error()
     assert ag(ptrs, 2, 1, M=65) == _lib.GFX_ERR_UNSUPPORTED and "M <= 64" in _lib.last_error()
     assert ag(ptrs, 2, 1, M=0) == _lib.GFX_OK  # M == 0: no launch
-    assert built_lib.gfx_peer_barrier(ctypes.cast(ptrs, ctypes.c_void_p), 2, -1, 1, None) == _lib.GFX_ERR_INVALID
-    assert built_lib.gfx_peer_barrier(ctypes.cast(nulls, ctypes.c_void_p), 2, 0, 1, None) == _lib.GFX_ERR_INVALID
+    assert built_lib.gfx_peer_barrier(ctypes.cast(ptrs, ctypes.c_void_p), 2, -1, None) == _lib.GFX_ERR_INVALID
+    assert built_lib.gfx_peer_barrier(ctypes.cast(nulls, ctypes.c_void_p), 2, 0, None) == _lib.GFX_ERR_INVALID
     assert "rank 1 is null" in _lib.last_error()

@@ -58,6 +58,22 @@ def _worker(rank, world, port, q):
         want = [split(x) for x in xs]
         out["fused_exact"] = all(torch.equal(a, b) for a, b in zip(got, want))
         out["fused_status"] = int(_lib.load().gfx_device_status(1))
+        # the same calls captured in a CUDA graph (two calls: the buffers keep alternating) and replayed
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fused(xs[0])
+            fused(xs[1])
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            g0, g1 = fused(xs[0]), fused(xs[1])
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        out["fused_graph_exact"] = bool(torch.equal(g0, want[0]) and torch.equal(g1, want[1]))
+        out["fused_graph_status"] = int(_lib.load().gfx_device_status(1))
+        del graph
         out["fused_vs_one"] = max(float((g.float() - lin(x).float()).abs().max() / lin(x).float().abs().max())
                                   for g, x in zip(got, xs))
         # token-row split of the same linear at large M (weights replicated)
@@ -100,6 +116,7 @@ def test_two_gpu_splits_match_one_gpu():
         # the channel split reorders nothing inside a dot product: fp32 rounding only
         assert val["channel_m1"] < 1e-2 and val["channel_m16"] < 1e-2, val
         assert val["fused_exact"] and val["fused_status"] == 0 and val["fused_vs_one"] < 1e-2, val
+        assert val["fused_graph_exact"] and val["fused_graph_status"] == 0, val
         assert val["tokens"] < 1e-6, val  # the same rows through the same kernel
         # bf16 activations through 4 blocks; the split changes only which GPU computes what
         assert val["batch"] < 2e-2 and val["rows"] < 2e-2, val
