@@ -17,9 +17,11 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Where the small-M kernel stores y: `count` copies (one per target buffer, for
 // example every rank's copy of a symmetric-memory buffer reached over NVLink),
-// each [M, ldy] with this launch's N columns starting at column col0. With
-// fence_sys set, every storing thread ends with a system-scope fence so that a
-// following cross-GPU barrier publishes the peer stores.
+// each [M, ldy] with this launch's N columns starting at column col0. A single
+// local target with fence_sys 0 runs the plain kernel (y = ptr[0], [M, N]);
+// anything else runs the all-gather variant, whose threads end with a
+// system-scope fence so that a following cross-GPU barrier publishes the peer
+// stores.
 constexpr int kMaxOutTargets = 8;
 struct OutTargets {
   void* ptr[kMaxOutTargets];

@@ -137,12 +137,19 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumerWarps * 32) : "memory");
 }
 
-// One output element to every target (the local y, or every rank's y).
-template <typename OutT>
-__device__ __forceinline__ void store_out(const OutTargets& out, int tok, int n, float v) {
+// One output element: into the local y [M, N] (restrict-qualified, so the
+// compiler may move the fix-up's loads across these stores), or, for the
+// all-gather variant, into every target buffer [M, ldy] at column col0 + n.
+template <typename OutT, bool kPeers>
+__device__ __forceinline__ void store_out(OutT* __restrict__ y, const OutTargets& out, int N, int tok, int n,
+                                          float v) {
   const OutT val = from_f32<OutT>(v);
-  const size_t off = (size_t)tok * out.ldy + out.col0 + n;
-  for (int q = 0; q < out.count; ++q) reinterpret_cast<OutT*>(out.ptr[q])[off] = val;
+  if constexpr (!kPeers) {
+    y[(size_t)tok * N + n] = val;
+  } else {
+    const size_t off = (size_t)tok * out.ldy + out.col0 + n;
+    for (int q = 0; q < out.count; ++q) reinterpret_cast<OutT*>(out.ptr[q])[off] = val;
+  }
 }
 
 // Token row of MMA column n within an 8-token tile (conflict-free activation loads).
@@ -153,12 +160,13 @@ __device__ __forceinline__ int owner_cta(long long t, long long U, int G) {
   return (int)(((t + 1) * G + U - 1) / U) - 1;
 }
 
-template <int NT, int STAGES, bool kF16Scale, typename OutT, bool kCl>
+template <int NT, int STAGES, bool kF16Scale, typename OutT, bool kCl, bool kPeers>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (NT == 2 ? GFX_SMALLM_CTAS_NT2 : 1))
     w4a16_smallm_kernel(
     const __grid_constant__ CUtensorMap nib_map, const __grid_constant__ CUtensorMap x_map,
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
-    const OutT* __restrict__ bias, const __grid_constant__ OutTargets out, float* __restrict__ partials,
+    const OutT* __restrict__ bias, OutT* __restrict__ y, const __grid_constant__ OutTargets out,
+    float* __restrict__ partials,
     int* __restrict__ counters,
     int M, int N, int K, int G, int max_segs) {
   using L = Layout<NT, STAGES, kF16Scale>;
@@ -439,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
               for (int cc = 0; cc < 2; ++cc) {
                 const int tok = tok0 + nt * 8 + tok_perm(2 * t_ + cc);
-                if (tok < M) store_out<OutT>(out, tok, n, acc[mt][nt][half * 2 + cc] + bv);
+                if (tok < M) store_out<OutT, kPeers>(y, out, N, tok, n, acc[mt][nt][half * 2 + cc] + bv);
               }
           }
       }
@@ -491,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
                   if (tok >= vt) continue;
                   float v = acc[mt][nt][half * 2 + cc];
                   for (uint32_t q = 1; q < csize; ++q) v += recv[((q - 1) * kTok + tok) * kRecvStride + r];
-                  store_out<OutT>(out, tok0 + tok, n, v + bv);
+                  store_out<OutT, kPeers>(y, out, N, tok0 + tok, n, v + bv);
                 }
             }
         }
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
             if (n >= N) continue;
             float o = vv[e];
             if (bias) o += to_f32(bias[n]);
-            store_out<OutT>(out, tok0 + tok, n, o);
+            store_out<OutT, kPeers>(y, out, N, tok0 + tok, n, o);
           }
         }
         if (tc == 0) *counter = 0;
@@ -572,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
   }
-  if (out.fence_sys) __threadfence_system();  // publish peer-buffer stores before a cross-GPU barrier
+  if constexpr (kPeers) __threadfence_system();  // publish peer-buffer stores before a cross-GPU barrier
   if constexpr (kCl) cluster_sync_all();  // no CTA of the cluster leaves while a peer may address it
 }
 
@@ -663,10 +671,10 @@ struct SmallMArgs {
   int M, N, K;
 };
 
-template <int NT, int STAGES, bool F16S, typename OutT, bool kCl>
+template <int NT, int STAGES, bool F16S, typename OutT, bool kCl, bool kPeers>
 static int launch_smallm_k(const SmallMPlan& p, const SmallMArgs& a, cudaStream_t st, int cluster) {
   using L = smallm::Layout<NT, STAGES, F16S>;
-  auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, kCl>;
+  auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, kCl, kPeers>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(p.G, p.tok_blocks);
@@ -685,7 +693,8 @@ static int launch_smallm_k(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
     cfg.numAttrs = 2;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
-                                     (const OutT*)a.bias, a.out, a.part, a.cnt, a.M, a.N, a.K, p.G, p.max_segs);
+                                     (const OutT*)a.bias, (OutT*)a.out.ptr[0], a.out, a.part, a.cnt, a.M, a.N, a.K,
+                                     p.G, p.max_segs);
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a16_smallm_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a16_smallm_kernel");
 }
@@ -709,7 +718,7 @@ static bool smallm_use_cluster(const SmallMPlan& p) {
   if (dev < 0 || dev >= 64) return false;
   int& m = max_active[dev][p.cl];
   if (m == 0) {
-    auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true>;
+    auto kern = smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true, false>;
     m = -1;
     if (p.cl > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
       (void)cudaGetLastError();
@@ -739,8 +748,9 @@ static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
   static bool attr_set[64] = {false};  // per device
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    for (auto kern : {smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, false>,
-                      smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true>}) {
+    for (auto kern : {smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, false, false>,
+                      smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, true, false>,
+                      smallm::w4a16_smallm_kernel<NT, STAGES, F16S, OutT, false, true>}) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
       if (e != cudaSuccess)
         return set_error(GFX_ERR_CUDA, "w4a16_smallm: cannot set %d bytes of shared memory: %s", L::kSmemBytes,
@@ -748,8 +758,10 @@ static int launch_smallm_t(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
     }
     attr_set[dev] = true;
   }
-  if (smallm_use_cluster<NT, STAGES, F16S, OutT>(p)) return launch_smallm_k<NT, STAGES, F16S, OutT, true>(p, a, st, p.cl);
-  return launch_smallm_k<NT, STAGES, F16S, OutT, false>(p, a, st, 1);
+  if (a.out.count > 1 || a.out.fence_sys) return launch_smallm_k<NT, STAGES, F16S, OutT, false, true>(p, a, st, 1);
+  if (smallm_use_cluster<NT, STAGES, F16S, OutT>(p))
+    return launch_smallm_k<NT, STAGES, F16S, OutT, true, false>(p, a, st, p.cl);
+  return launch_smallm_k<NT, STAGES, F16S, OutT, false, false>(p, a, st, 1);
 }
 
 template <int NT, int STAGES, bool F16S>
