@@ -23,7 +23,7 @@ import math
 import torch
 import torch.nn.functional as F
 
-from .ops import Gfx906Int4Ops
+from .ops import Gfx906Int4Ops, int4_linear, int4_linear_w4a4
 
 
 @dataclasses.dataclass
@@ -165,10 +165,36 @@ class Modulation(torch.nn.Module):
 class AttentionExchange:
     """How a block's attention sees keys/values. The default is local (all
     tokens on this device). ``parallel.TokenShard`` replaces it to gather the
-    image keys/values of every rank."""
+    image keys/values of every rank.
+
+    ``start(img_k, img_v)`` begins the exchange and ``finish(pending, txt_k,
+    txt_v)`` returns the joint keys and values; a block computes independent
+    work (the next linear) between the two, so a remote exchange overlaps it.
+    ``overlaps`` tells a block whether restructuring its work for that pays."""
+
+    overlaps = False
+
+    def start(self, img_k, img_v):
+        return img_k, img_v
+
+    def finish(self, pending, txt_k, txt_v):
+        img_k, img_v = pending
+        return torch.cat([txt_k, img_k], dim=2), torch.cat([txt_v, img_v], dim=2)
 
     def joint_kv(self, txt_k, txt_v, img_k, img_v):
-        return torch.cat([txt_k, img_k], dim=2), torch.cat([txt_v, img_v], dim=2)
+        return self.finish(self.start(img_k, img_v), txt_k, txt_v)
+
+
+def linear_rows(lin, x, r0: int, r1: int):
+    """Output features [r0, r1) of ``lin(x)``: the same layer restricted to
+    those weight rows (row slices of the packed weight, no copy), so a fused
+    linear can be computed in parts."""
+    b = lin.bias[r0:r1].to(x.dtype) if lin.bias is not None else None
+    if isinstance(lin, Gfx906Int4Ops.Linear) and lin.quantized:
+        scale = lin._device_scale(lin.weight_scale)[r0:r1]
+        fn = int4_linear_w4a4 if lin.activation_quant else int4_linear
+        return fn(x, lin.weight_q4[r0:r1], scale, b, lin.rotation_group)
+    return F.linear(x, lin.weight[r0:r1].to(x.dtype), b)
 
 
 def attention(q, k, v):
@@ -209,10 +235,11 @@ class DoubleBlock(torch.nn.Module):
         im = self.img_mod(vec)
         tm = self.txt_mod(vec)
         iq, ik, iv = self._qkv(img, im[0:2], self.img_qkv, self.img_qn, self.img_kn)
-        tq, tk, tv = self._qkv(txt, tm[0:2], self.txt_qkv, self.txt_qn, self.txt_kn)
         iq, ik = apply_rope(iq, pe_img), apply_rope(ik, pe_img)
+        pending = ex.start(ik, iv)  # the image K/V exchange runs while the text stream's linear computes
+        tq, tk, tv = self._qkv(txt, tm[0:2], self.txt_qkv, self.txt_qn, self.txt_kn)
         tq, tk = apply_rope(tq, pe_txt), apply_rope(tk, pe_txt)
-        k, v = ex.joint_kv(tk, tv, ik, iv)
+        k, v = ex.finish(pending, tk, tv)
         o = attention(torch.cat([tq, iq], dim=2), k, v)
         Lt = txt.shape[1]
         t_o, i_o = _merge(o[:, :, :Lt]), _merge(o[:, :, Lt:])
@@ -238,15 +265,24 @@ class SingleBlock(torch.nn.Module):
 
     def forward(self, x, vec, Lt, pe_txt, pe_img, ex: AttentionExchange):
         shift, scale, gate = self.mod(vec)
-        y = self.lin1((1 + scale) * layer_norm(x) + shift)
+        xin = (1 + scale) * layer_norm(x) + shift
         h = x.shape[-1]
-        qkv, mlp = y[..., : 3 * h], y[..., 3 * h:]
+        if ex.overlaps:
+            # the fused linear in two parts: the q/k/v rows, then (while the
+            # image K/V exchange runs) the MLP rows
+            qkv, mlp = linear_rows(self.lin1, xin, 0, 3 * h), None
+        else:
+            y = self.lin1(xin)
+            qkv, mlp = y[..., : 3 * h], y[..., 3 * h:]
         q, k, v = qkv.chunk(3, dim=-1)
         q, k, v = _heads(q, self.heads), _heads(k, self.heads), _heads(v, self.heads)
         q, k = self.qn(q), self.kn(k)
         pe = torch.cat([pe_txt, pe_img], dim=2)
         q, k = apply_rope(q, pe), apply_rope(k, pe)
-        kk, vv = ex.joint_kv(k[:, :, :Lt], v[:, :, :Lt], k[:, :, Lt:], v[:, :, Lt:])
+        pending = ex.start(k[:, :, Lt:], v[:, :, Lt:])
+        if mlp is None:
+            mlp = linear_rows(self.lin1, xin, 3 * h, 3 * h + self.mlp)
+        kk, vv = ex.finish(pending, k[:, :, :Lt], v[:, :, :Lt])
         o = _merge(attention(q, kk, vv))
         return x + gate * self.lin2(torch.cat([o, F.gelu(mlp, approximate="tanh")], dim=-1))
 

@@ -11,8 +11,9 @@ and PCIe copies, for any world size that divides the work.
   * Token-row split (row_split.py:191-206): the image tokens of one sample are
     split into G contiguous blocks of latent rows; every rank keeps all text
     tokens. Each block's attention gathers the image keys and values of all
-    ranks with one ``all_gather_into_tensor`` per tensor (the reference swaps
-    K/V with its peer, row_split.py:47-64,87-96); queries stay local, so the
+    ranks with one asynchronous ``all_gather_into_tensor`` per tensor,
+    overlapped with the block's next linear (the reference swaps K/V with its
+    peer, row_split.py:47-64,87-96); queries stay local, so the
     int4 linears only ever see the rank's own tokens. Text keys come from the
     rank's own (replicated) text stream, so they count once (the reference
     drops rank 1's copy, row_split.py:90-94). RoPE uses each token's true row
@@ -44,22 +45,34 @@ def _log_plan(kind: str, **plan):
 
 
 class TokenShard(AttentionExchange):
-    """Gathers the image keys/values of every rank (rank order = token order)."""
+    """Gathers the image keys/values of every rank (rank order = token order).
+
+    ``start`` issues both all-gathers asynchronously (NCCL runs them on its own
+    stream) and ``finish`` waits for them, so the linear a block computes in
+    between overlaps the exchange."""
+
+    overlaps = True
 
     def __init__(self, group=None):
         self.group = group
         self.world = dist.get_world_size(group)
 
-    def _gather(self, t: torch.Tensor) -> torch.Tensor:
-        # t [B, H, L_local, D] -> [B, H, L_local * world, D], rank-major along L
-        t = t.contiguous()
-        B, H, L, D = t.shape
-        out = torch.empty(self.world * B, H, L, D, dtype=t.dtype, device=t.device)  # dim-0 concatenation
-        dist.all_gather_into_tensor(out, t, group=self.group)
-        return out.view(self.world, B, H, L, D).permute(1, 2, 0, 3, 4).reshape(B, H, self.world * L, D)
+    def start(self, img_k, img_v):
+        pending = []
+        for t in (img_k, img_v):
+            t = t.contiguous()
+            out = torch.empty(self.world * t.shape[0], *t.shape[1:], dtype=t.dtype, device=t.device)
+            work = dist.all_gather_into_tensor(out, t, group=self.group, async_op=True)  # dim-0 concatenation
+            pending.append((out, work, t.shape))
+        return pending
 
-    def joint_kv(self, txt_k, txt_v, img_k, img_v):
-        return torch.cat([txt_k, self._gather(img_k)], dim=2), torch.cat([txt_v, self._gather(img_v)], dim=2)
+    def finish(self, pending, txt_k, txt_v):
+        full = []
+        for out, work, (B, H, L, D) in pending:
+            work.wait()
+            # [world * B, H, L, D] -> [B, H, world * L, D], rank-major along L
+            full.append(out.view(self.world, B, H, L, D).permute(1, 2, 0, 3, 4).reshape(B, H, self.world * L, D))
+        return torch.cat([txt_k, full[0]], dim=2), torch.cat([txt_v, full[1]], dim=2)
 
 
 def row_block(h_tokens: int, rank: int, world: int):

@@ -202,6 +202,25 @@ def test_gemm_large_m_tcgen05(cuda, M, N, K, f16_scales):
     _check(ybf.float().cpu().numpy(), O.w4a16_matmul(xn, p, s))
 
 
+@pytest.mark.parametrize("M", [1, 9, 64, 65, 300])
+def test_gemm_single_group_k32(cuda, M):
+    """K = 32: one scale group per row, narrower than every tile's K extent
+    (TMA fills the rest of the box with zeros) and a scale row of 4 bytes
+    (not TMA-aligned, so the scales come through cp.async); both kernels, on
+    either side of the M = 64 switch, with a ragged N. Each kernel is held
+    tight against the oracle of its own arithmetic: the small-M kernel scales
+    exact integer-code partials in fp32 (fp32 dequant oracle), the tensor-core
+    kernel multiplies bf16(code * scale) (bf16-weight oracle)."""
+    N, K = 130, 32
+    p, s, pd, sd = _weights(N, K, seed=33, dev=cuda)
+    xn, xd = _x(M, K, seed=34 + M, dev=cuda)
+    bias = torch.linspace(-1, 1, N, device=cuda)
+    y32 = ops.gemm_w4a16(xd, pd, sd, bias, torch.float32).cpu().numpy()
+    exact = O.w4a16_matmul(xn, p, s) if M <= 64 else O.w4a16_matmul_bf16w(xn, p, s)
+    _check(y32, exact + bias.cpu().numpy(), 1e-5, 1e-5)
+    _check(y32, O.w4a16_matmul(xn, p, s) + bias.cpu().numpy())
+
+
 def test_gemm_large_m_general_fp32_scales(cuda):
     N, K, M = 520, 1024, 400
     w = synthetic.float_weight(N, K, 31)
