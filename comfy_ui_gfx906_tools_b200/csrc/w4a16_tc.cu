@@ -71,6 +71,10 @@ constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6,
 // Dequant warp groups working on different stages at once (1, 2, 4 or 8).
 constexpr int kDeqGroups = GFX_TC_DEQ_GROUPS;
 static_assert(kDeqGroups == 1 || kDeqGroups == 2 || kDeqGroups == 4 || kDeqGroups == 8, "bad dequant grouping");
+#ifndef GFX_TC_SPLIT_NIB
+#define GFX_TC_SPLIT_NIB 0
+#endif
+constexpr uint32_t kNibLead = 4;  // stages the nibble ring runs ahead of the x tiles
 constexpr int kAccCols = kTileM;  // fp32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kWBytes = kTileN * kStageK * 2;  // 16 KB
@@ -95,10 +99,19 @@ struct Traits {
   static constexpr int kQRowBytes = kInt8 ? kStageK : kStageK / 2;  // packed bytes per row per stage
   static constexpr int kQBytes = kTileN * kQRowBytes;
   static constexpr int kScaleBytes = kChannel ? 0 : 1024;            // 128 rows x 2 groups x <= 4 B
-  static constexpr int kStageBytes = kXBytes + kWBytes + kQBytes + kScaleBytes;
-  static constexpr int kFit = (kSmemLimit - 1024 - kBarrierBytes) / kStageBytes;
+  // int4 on one CTA: the packed weights and scales have a ring of their own
+  // (kNibSlots slots, loaded up to kNibLead stages ahead of the x tiles), so
+  // the dequant of a stage waits for its nibbles and a free weight slot only,
+  // never for the 32 KB x tile; the x TMA and the dequant then overlap instead
+  // of running one after the other in each ring slot.
+  static constexpr bool kSplit = C == 1 && !kInt8 && GFX_TC_SPLIT_NIB != 0;
+  static constexpr int kNibSlotBytes = kQBytes + kScaleBytes;         // 5 KB for int4
+  static constexpr int kNibSlots = kSplit ? 6 : 0;
+  static constexpr int kStageBytes = kXBytes + kWBytes + (kSplit ? 0 : kQBytes + kScaleBytes);
+  static constexpr int kFit = (kSmemLimit - 1024 - kBarrierBytes - kNibSlots * kNibSlotBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNibSlots * kNibSlotBytes + kBarrierBytes;
+  static_assert(kNibSlotBytes % 1024 == 0, "nibble slots must stay 1024-byte aligned");
   static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-byte aligned");
   static_assert(kStages >= 3, "pipeline too shallow");
 };
@@ -273,6 +286,9 @@ struct Smem {
   uint64_t* acc_full;  // [2]
   uint64_t* acc_empty; // [2]
   uint64_t* drain;     // [1]
+  uint8_t* nib0;       // split ring: slot n starts at nib0 + n * kNibSlotBytes
+  uint64_t* nfull;     // [kNibSlots] nibbles + scales landed
+  uint64_t* nempty;    // [kNibSlots] the dequant is done reading the slot
   uint32_t* tmem_base;
 };
 
@@ -291,18 +307,23 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   // full[s] is exact only if the load kStages iterations earlier (the same
   // group's previous item on that stage) has already landed.
   constexpr int kG = kStages % kDeqGroups == 0 ? kDeqGroups : (kStages % 2 == 0 ? 2 : 1);
+  static_assert(!T::kSplit || T::kNibSlots % kG == 0, "a dequant group must own fixed nibble slots");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Smem sm;
   sm.stage0 = base;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+  sm.nib0 = base + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.nib0 + T::kNibSlots * T::kNibSlotBytes);
   sm.full = bars;
   sm.wready = bars + kStages;
   sm.empty = bars + 2 * kStages;
   sm.acc_full = bars + 3 * kStages;
   sm.acc_empty = bars + 3 * kStages + 2;
   sm.drain = bars + 3 * kStages + 4;
-  sm.tmem_base = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 5);
+  sm.nfull = bars + 3 * kStages + 5;
+  sm.nempty = sm.nfull + T::kNibSlots;
+  sm.tmem_base = reinterpret_cast<uint32_t*>(sm.nempty + T::kNibSlots);
+  static_assert((3 * kStages + 5 + 2 * T::kNibSlots) * 8 + 4 <= kBarrierBytes, "barrier area");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -317,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], T::kChannel ? 1 : 1 + 32);
+      mbar_init(&sm.full[s], (T::kChannel || T::kSplit) ? 1 : 1 + 32);
       mbar_init(&sm.wready[s], kDequantWarps / kG * C);  // one group; a pair's arrive on CTA 0
       mbar_init(&sm.empty[s], 1);
     }
@@ -326,6 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
       mbar_init(&sm.acc_empty[a], kEpiWarps * C);
     }
     mbar_init(sm.drain, 1);
+    for (int n = 0; n < T::kNibSlots; ++n) {
+      mbar_init(&sm.nfull[n], 1 + 32);
+      mbar_init(&sm.nempty[n], kDequantWarps / kG);
+    }
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<C>(sm.tmem_base, kTmemCols);
@@ -354,45 +379,83 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
       }
     }
     pdl_wait();
-    uint32_t kit = 0;
-    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
-      const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
-      const int m0 = (tile / tiles_n) * kTileM + (int)cr * T::kXRows;
-      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
-        const int s = kit % kStages;
-        const uint32_t ph = (kit / kStages) & 1;
-        if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
-        uint8_t* st = sm.stage0 + s * kStageBytes;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
-          tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
-          tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
-        }
-        if constexpr (!T::kChannel) {
-          uint8_t* sc = st + kXBytes + kWBytes + T::kQBytes;
-          const int g0 = ks * 2;
-          if constexpr (T::kF16Group) {
-            // one 4-byte word = the two fp16 scales of a row; smem layout [row]
+    // per-row group scales of K stage ks for rows n0.. into sc (cp.async), then
+    // one no-increment arrival of this thread on bar when they have landed
+    auto load_scales = [&](uint8_t* sc, int n0, int ks, uint64_t* bar) {
+      if constexpr (!T::kChannel) {
+        const int g0 = ks * 2;
+        if constexpr (T::kF16Group) {
+          // one 4-byte word = the two fp16 scales of a row; smem layout [row]
 #pragma unroll
-            for (int j = 0; j < kTileN / 32; ++j) {
-              const int r = lane + 32 * j, n = n0 + r;
-              const bool valid = n < N && g0 < groups;
-              const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-              if (valid) src += ((size_t)n * groups + g0) * 2;
-              cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
-            }
-          } else {
-            // fp32, smem layout [group][row] (conflict-free reads)
-#pragma unroll
-            for (int j = 0; j < 2 * kTileN / 32; ++j) {
-              const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
-              const bool valid = n < N && (g0 + g) < groups;
-              const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-              if (valid) src += ((size_t)n * groups + g0 + g) * 4;
-              cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
-            }
+          for (int j = 0; j < kTileN / 32; ++j) {
+            const int r = lane + 32 * j, n = n0 + r;
+            const bool valid = n < N && g0 < groups;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+            if (valid) src += ((size_t)n * groups + g0) * 2;
+            cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
           }
-          cp_async_mbar_arrive_noinc(&sm.full[s]);
+        } else {
+          // fp32, smem layout [group][row] (conflict-free reads)
+#pragma unroll
+          for (int j = 0; j < 2 * kTileN / 32; ++j) {
+            const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
+            const bool valid = n < N && (g0 + g) < groups;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
+            if (valid) src += ((size_t)n * groups + g0 + g) * 4;
+            cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
+          }
+        }
+        cp_async_mbar_arrive_noinc(bar);
+      }
+    };
+    if constexpr (T::kSplit) {
+      // stage kit of this CTA = K stage kit % k_stages of its (kit / k_stages)-th tile
+      const int my_tiles = first_tile < num_tiles ? (num_tiles - first_tile + tile_step - 1) / tile_step : 0;
+      const uint32_t total = (uint32_t)my_tiles * (uint32_t)k_stages;
+      uint32_t nk = 0;
+      for (uint32_t kit = 0; kit < total && ok; ++kit) {
+        for (; nk < total && nk <= kit + kNibLead; ++nk) {
+          const int n = nk % T::kNibSlots;
+          if (!mbar_wait(&sm.nempty[n], ((nk / T::kNibSlots) & 1) ^ 1, kDevErrEmptyBarrierTimeout)) {
+            ok = false;
+            break;
+          }
+          const int tile = first_tile + (int)(nk / k_stages) * tile_step;
+          const int ks = nk % k_stages;
+          const int n0 = (tile % tiles_n) * kTileN;
+          uint8_t* qs = sm.nib0 + n * T::kNibSlotBytes;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&sm.nfull[n], T::kQBytes);
+            tma_load_2d(qs, &q_map, &sm.nfull[n], ks * T::kQRowBytes, n0);
+          }
+          load_scales(qs + T::kQBytes, n0, ks, &sm.nfull[n]);
+        }
+        if (!ok) break;
+        const int s = kit % kStages;
+        if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+        const int tile = first_tile + (int)(kit / k_stages) * tile_step;
+        const int m0 = (tile / tiles_n) * kTileM;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.full[s], kXBytes);
+          tma_load_2d(sm.stage0 + s * kStageBytes, &x_map, &sm.full[s], (int)(kit % k_stages) * kStageK, m0);
+        }
+      }
+    } else {
+      uint32_t kit = 0;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+        const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
+        const int m0 = (tile / tiles_n) * kTileM + (int)cr * T::kXRows;
+        for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+          const int s = kit % kStages;
+          const uint32_t ph = (kit / kStages) & 1;
+          if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+          uint8_t* st = sm.stage0 + s * kStageBytes;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
+            tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
+            tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
+          }
+          load_scales(st + kXBytes + kWBytes + T::kQBytes, n0, ks, &sm.full[s]);
         }
       }
     }
@@ -412,9 +475,23 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
         if ((int)(kit % kG) != q) continue;
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
-        if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
         uint8_t* st = sm.stage0 + s * kStageBytes;
-        const uint8_t* qt = st + kXBytes + kWBytes;
+        const uint8_t* qt;
+        int nslot = 0;
+        if constexpr (T::kSplit) {
+          // its nibbles and scales have landed, and the MMAs that read this
+          // stage's weight slot kStages stages ago are done
+          nslot = kit % T::kNibSlots;
+          if (!mbar_wait(&sm.nfull[nslot], (kit / T::kNibSlots) & 1, kDevErrFullBarrierTimeout) ||
+              !mbar_wait(&sm.empty[s], ph ^ 1, kDevErrMmaBarrierTimeout)) {
+            ok = false;
+            break;
+          }
+          qt = sm.nib0 + nslot * T::kNibSlotBytes;
+        } else {
+          if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
+          qt = st + kXBytes + kWBytes;
+        }
         const uint8_t* sc = qt + T::kQBytes;
 #pragma unroll
         for (int item_j = 0; item_j < kG; ++item_j) {
@@ -464,6 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
           // this CTA's x slice and dequantized rows of stage s are in place
           if constexpr (C == 1) {
             mbar_arrive(&sm.wready[s]);
+            if constexpr (T::kSplit) mbar_arrive(&sm.nempty[nslot]);  // the nibble slot may be refilled
           } else {
             mbar_arrive_cluster(&sm.wready[s], 0);
           }
