@@ -103,7 +103,9 @@ struct Traits {
   // (kNibSlots slots, loaded up to kNibLead stages ahead of the x tiles), so
   // the dequant of a stage waits for its nibbles and a free weight slot only,
   // never for the 32 KB x tile; the x TMA and the dequant then overlap instead
-  // of running one after the other in each ring slot.
+  // of running one after the other in each ring slot. Off by default: on B200
+  // it measured ~20% slower (772 vs 963-972 TFLOP/s over the six Flux shapes
+  // at M = 4608; every parity test passes with it on).
   static constexpr bool kSplit = C == 1 && !kInt8 && GFX_TC_SPLIT_NIB != 0;
   static constexpr int kNibSlotBytes = kQBytes + kScaleBytes;         // 5 KB for int4
   static constexpr int kNibSlots = kSplit ? 6 : 0;
