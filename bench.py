@@ -1,26 +1,35 @@
 """Benchmark of the int4 W4A16 linear path on B200 (driver contract: one JSON line).
 
-Workload (config 2, "flux_linear_sweep"): one step = the six Flux DiT
-linear shapes at hidden 3072 ((K, N) in qkv 3072x9216, proj 3072x3072, mlp-up
+Workload (config 2, "flux_linear_sweep"): one step = the six Flux DiT linear
+shapes at hidden 3072 ((K, N) in qkv 3072x9216, proj 3072x3072, mlp-up
 3072x12288, mlp-down 12288x3072, single-fused 3072x21504, single-out
 15360x3072), M = 4608 tokens each, bf16 activations, int4 group-32 weights
 from synthetic ggml Q4_0 blocks, bf16 output. metric = whole-job TFLOP/s
 (2*M*N*K per GEMM). Each step reads > 126 MB (L2) of distinct inputs, so the
-timed loop does not run out of L2. The M in {1, 16} variants of the same
-weights are reported as GB/s of algorithmic bytes in "small_m".
+timed loop does not run out of L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --case qkv --m 1 [--reps 20] [--graph] [--copies 3]   (one GEMM shape, for ncu / quick timing)
 
-N > 1 runs under torchrun: every rank runs the same per-GPU workload (its own
-4608 tokens; weak scaling, no data-path collective), timing is the max over
-ranks of CUDA-event time. --impl reference times the reference's CPU torch
-path (dequant + fp32 matmul; the oracle's torch port) on this host's cores.
+N = 1: the whole 4608-token sweep on one GPU. N > 1 (torchrun, one rank per
+GPU, NCCL): the same fixed workload split by token rows (rank r computes rows
+[r*M/N, (r+1)*M/N) of every GEMM, weights replicated) with one
+all_gather_into_tensor of each GEMM's output inside the timed region,
+overlapped with the next GEMM (strong scaling); timing is the max over ranks
+of CUDA-event time, and a "parity" key compares the gathered output with the
+same GEMMs run whole on one GPU and with a torch fp32 dequant-then-matmul.
+The M in {1, 16} variants of the same weights are reported as GB/s of
+algorithmic bytes in "small_m" (output-channel split at N > 1), the int8
+config-3 sweep in "int8", the row-split DiT forward (config 5) in "dit_rows".
+--impl reference times the reference's CPU torch path (dequant + fp32 matmul,
+the oracle's torch port) on this host's cores, full size.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import platform
 import subprocess
 import sys
 import tempfile
@@ -35,6 +44,7 @@ SHAPES = [("qkv", 3072, 9216), ("proj", 3072, 3072), ("mlp_up", 3072, 12288), ("
           ("single_fused", 3072, 21504), ("single_out", 15360, 3072)]
 METRIC = "int4 W4A16 GEMM TFLOP/s at M=4608 over the six Flux linear shapes"
 UNIT = "TFLOP/s"
+M_FULL = 4608
 
 
 def peaks():
@@ -44,6 +54,15 @@ def peaks():
         return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
                 "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def workload_config(world: int) -> dict:
+    """The `config` of both arms' JSON lines (identical for a given N)."""
+    return {"workload": "flux_linear_sweep", "M": M_FULL, "shapes": [s[0] for s in SHAPES],
+            "weights": "int4 group-32, ggml Q4_0 synthetic (fp16-exact scales)",
+            "l2": "each step reads > 126 MB of distinct inputs (no flush needed)",
+            "parallelism": ("single GPU" if world == 1 else
+                            f"token rows / {world} (weights replicated), all_gather_into_tensor of y timed")}
 
 
 class ClockSampler:
@@ -99,7 +118,7 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def setup_dist(n_gpus):
+def setup_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -127,54 +146,110 @@ def max_over_ranks(v, world, dev):
     return float(t.item())
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(shape_idx, rows, seed=0):
-    """Reference CPU torch path on one shape: full dequant + fp32 matmul of `rows`
-    tokens; returns (t_dequant, t_matmul, flops_extrapolated_to_4608, seconds_extrapolated)."""
+# the reference's CPU torch path (the oracle's torch port), full size
+# ---------------------------------------------------------------------------
+def cpu_reference_inputs(seed=0):
+    """Native int4 weights of the six shapes (the reference's own repack of the
+    same synthetic Q4_0 blocks) and the M=4608 activations, on the CPU."""
     import oracle as O
     from comfy_ui_gfx906_tools_b200 import synthetic
-    name, K, N = SHAPES[shape_idx]
-    raw, _, _ = synthetic.q4_0_weight(N, K, seed=seed + shape_idx)
-    p, s = O.repack_q4_0_native(raw.numpy(), N, K)
-    pt, st = torch.from_numpy(p), torch.from_numpy(s)
-    x = synthetic.activations(rows, K, seed=seed + 50)
-    t0 = time.perf_counter()
-    w = O.torch_cpu_dequant(pt, st)
-    t1 = time.perf_counter()
-    y = torch.matmul(x.float(), w.t())
-    t2 = time.perf_counter()
-    del y
-    t_dq, t_mm = t1 - t0, t2 - t1
-    M = 4608
-    return t_dq, t_mm, 2.0 * M * N * K, t_dq + t_mm * (M / rows)
+    out = []
+    for i, (name, K, N) in enumerate(SHAPES):
+        raw, _, _ = synthetic.q4_0_weight(N, K, seed=seed + i)
+        p, s = O.repack_q4_0_native(raw.numpy(), N, K)
+        x = synthetic.activations(M_FULL, K, seed=seed + 50 + i)
+        out.append((name, K, N, torch.from_numpy(p), torch.from_numpy(s), x))
+    return out
+
+
+def cpu_reference_step(inputs, M=M_FULL):
+    """One full sweep of the reference CPU path: per shape the torch dequant
+    (int4_train_test.py:46-52) then the fp32 matmul of M rows (bench_int8.py:43),
+    timed separately. Returns {shape: (t_dequant, t_matmul)}."""
+    import oracle as O
+    times = {}
+    for name, K, N, p, s, x in inputs:
+        xf = x[:M].float()
+        t0 = time.perf_counter()
+        w = O.torch_cpu_dequant(p, s)
+        t1 = time.perf_counter()
+        y = torch.matmul(xf, w.t())
+        t2 = time.perf_counter()
+        del y, w
+        times[name] = (t1 - t0, t2 - t1)
+    return times
+
+
+def cpu_baseline_best_of(reps=3):
+    """cpu_baseline: the six shapes at M=4608, dequant and matmul timed
+    separately, best of `reps` per shape and phase; plus M in {1, 16} as GB/s."""
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    inputs = cpu_reference_inputs()
+    best = {}
+    for _ in range(reps):
+        for name, (tdq, tmm) in cpu_reference_step(inputs).items():
+            b = best.get(name, (float("inf"), float("inf")))
+            best[name] = (min(b[0], tdq), min(b[1], tmm))
+    flops = sum(2.0 * M_FULL * N * K for (_, K, N) in SHAPES)
+    t_total = sum(a + b for a, b in best.values())
+    small = {}
+    for Ms in (1, 16):
+        bs = {}
+        for _ in range(reps):
+            for name, (tdq, tmm) in cpu_reference_step(inputs, Ms).items():
+                bs[name] = min(bs.get(name, float("inf")), tdq + tmm)
+        nbytes = sum(N * K // 2 + N * (K // 32) * 4 + Ms * K * 2 + Ms * N * 2 for (_, K, N) in SHAPES)
+        small[f"M{Ms}"] = {"GB_s": nbytes / sum(bs.values()) / 1e9, "s_per_sweep": sum(bs.values())}
+    return {"value": flops / t_total / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": "the full workload: six Flux shapes at M=4608, torch-CPU dequant of each weight and fp32 "
+                      f"matmul timed separately, best of {reps} per shape and phase (no extrapolation)",
+            "per_shape_s": {k: {"dequant": v[0], "matmul": v[1]} for k, v in best.items()},
+            "dequant_s": sum(v[0] for v in best.values()), "matmul_s": sum(v[1] for v in best.values()),
+            "small_m": small}
 
 
 def run_reference(args, world, rank):
+    """--impl reference: the reference CPU path on the whole workload, one full
+    six-shape sweep at M=4608 per step, on rank 0 only."""
     if rank != 0:
         return
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    rows = 256
-    for i in range(args.warmup):
-        cpu_reference_sample(i % len(SHAPES), rows)
-    flops = secs = 0.0
-    t_start = time.perf_counter()
-    for i in range(args.steps):
-        _, _, f, s = cpu_reference_sample(i % len(SHAPES), rows)
-        flops += f
-        secs += s
-    wall = time.perf_counter() - t_start
-    value = flops / secs / 1e12
-    sample = (f"per step one Flux shape (round-robin): full torch-CPU dequant of W + fp32 matmul of {rows} of the "
-              f"4608 rows, extrapolated to M=4608 as t_dequant + t_matmul*4608/{rows}")
+    inputs = cpu_reference_inputs()
+    flops = sum(2.0 * M_FULL * N * K for (_, K, N) in SHAPES)
+    for _ in range(args.warmup):
+        cpu_reference_step(inputs)
+    secs = 0.0
+    dq = mm = 0.0
+    for _ in range(args.steps):
+        t = cpu_reference_step(inputs)
+        secs += sum(a + b for a, b in t.values())
+        dq += sum(a for a, _ in t.values())
+        mm += sum(b for _, b in t.values())
+    value = args.steps * flops / secs / 1e12
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "flux_linear_sweep", "M": 4608, "shapes": [s[0] for s in SHAPES]},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+                         "sample": "each step the full workload: six Flux shapes at M=4608, torch-CPU dequant + "
+                                   "fp32 matmul (the reference's CPU torch path), no extrapolation",
+                         "dequant_s_per_step": dq / args.steps, "matmul_s_per_step": mm / args.steps},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": wall,
     }))
 
 
@@ -213,62 +288,101 @@ def time_steps(fn, steps, warmup, world, dev, stream, soak_s=0.0):
     return a.elapsed_time(b)
 
 
+def parity_of(got: torch.Tensor, ref: torch.Tensor) -> dict:
+    d = (got.double() - ref.double()).abs()
+    r = ref.double().abs()
+    return {"max_abs_over_max_ref": float(d.max() / r.max()), "mean_rel": float(d.mean() / r.mean()),
+            "nonfinite": int((~torch.isfinite(got)).sum())}
+
+
+def torch_reference_rows(x, p, s, rows):
+    """fp32 dequant-then-matmul of the sampled rows in torch on the GPU (the
+    bit-exact dequant kernel, then a plain fp32 matmul)."""
+    from comfy_ui_gfx906_tools_b200 import ops
+    w = ops.dequantize_int4(p, s, torch.float32)
+    return x[rows].float() @ w.t()
+
+
 def run_ours(args, world, rank, local):
     from comfy_ui_gfx906_tools_b200 import ops, synthetic
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
     pk = peaks()
-    M = args.m
+    M = M_FULL
+    per = M // world
+    r0 = rank * per
     weights = make_weights(dev, seed=1000)
     xs = [synthetic.activations(M, K, seed=2000 + i).to(dev) for i, (_, K, _, _, _) in enumerate(weights)]
+    xloc = [x[r0:r0 + per].contiguous() for x in xs]
     flops_step = sum(2.0 * M * N * K for (_, K, N, _, _) in weights)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    yfull = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for (_, _, N, _, _) in weights] if world > 1 else None
 
-    # --- device-resident timed loop, with per-launch events for the roofline ---
+    # --- device-resident timed loop ---
     launch_ms = [0.0] * len(weights)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in weights]
     record = {"on": False}
 
     def step():
-        for i, ((_, K, N, p, s), x) in enumerate(zip(weights, xs)):
+        works = []
+        for i, ((_, K, N, p, s), x) in enumerate(zip(weights, xloc)):
             if record["on"]:
                 ev[i][0].record(stream)
-            ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+            y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
             if record["on"]:
                 ev[i][1].record(stream)
-
-    def timed_step():
-        step()
-        torch.cuda.synchronize(dev)
-        for i in range(len(weights)):
-            launch_ms[i] += ev[i][0].elapsed_time(ev[i][1])
+            if world > 1:  # this GEMM's rows to every rank, overlapped with the next GEMM
+                works.append(dist.all_gather_into_tensor(yfull[i], y, async_op=True))
+        for w in works:
+            w.wait()
 
     clocks = ClockSampler(dev.index)
     with clocks:
         ms_total = time_steps(step, args.steps, args.warmup, world, dev, stream, soak_s=1.0)
     ms_total = max_over_ranks(ms_total, world, dev)
     ms_step = ms_total / args.steps
-    value = world * flops_step / (ms_step * 1e-3) / 1e12
-    # per-launch durations, measured on the launching stream in a second pass
+    value = flops_step / (ms_step * 1e-3) / 1e12
+    # per-launch kernel durations on the launching stream, in a second pass
     record["on"] = True
     for _ in range(args.steps):
-        timed_step()
+        step()
+        torch.cuda.synchronize(dev)
+        for i in range(len(weights)):
+            launch_ms[i] += ev[i][0].elapsed_time(ev[i][1])
     record["on"] = False
     avg_launch_ms = sum(launch_ms) / (args.steps * len(weights))
-    achieved = (flops_step / len(weights)) / (avg_launch_ms * 1e-3) / 1e12
-    peak = pk["bf16_tflops_sustained"]
+    achieved = (flops_step / world / len(weights)) / (avg_launch_ms * 1e-3) / 1e12
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
         traffic = json.load(open(tf)).get("w4a16_large_m")
 
+    # --- parity of the timed step's output: sampled rows against a torch fp32
+    # dequant-then-matmul, and (N > 1) the gathered rows against the whole
+    # GEMM on one GPU ---
+    parity = {}
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(5))[:64].sort().values.to(dev)
+    for i, ((name, K, N, p, s), x) in enumerate(zip(weights, xs)):
+        y = yfull[i] if world > 1 else ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+        ent = parity_of(y[rows].float(), torch_reference_rows(x, p, s, rows))
+        if world > 1:
+            whole = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+            ent["vs_one_gpu"] = parity_of(y.float(), whole.float())
+            ent["bit_identical_to_one_gpu"] = bool(torch.equal(y, whole))
+            del whole
+        parity[name] = ent
+    parity_ok = all(e["max_abs_over_max_ref"] <= 2e-2 and e["mean_rel"] <= 5e-3 and e["nonfinite"] == 0
+                    for e in parity.values())
+
     # --- small M (HBM bound): GB/s of algorithmic bytes, CUDA-graph replay, rotated weight copies ---
     small = {}
-    if not args.no_small:
+    if not args.no_small and world == 1:
         copies = [weights] + [make_weights(dev, seed=3000 + 100 * c) for c in range(2)]
         for Ms in (1, 16):
             xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev) for i, (_, K, _, _, _) in enumerate(weights)]
-            outs = []
 
             def small_pass():
                 for cp in copies:
@@ -289,8 +403,7 @@ def run_ours(args, world, rank, local):
                     nbytes += N * K // 2 + N * (K // 32) * s.element_size() + Ms * K * 2 + Ms * N * 2
             reps = 20
             ms = time_steps(g.replay, reps, 3, world, dev, stream) / reps
-            ms = max_over_ranks(ms, world, dev)
-            small[f"M{Ms}"] = {"GB_s": world * nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (3 * len(weights)),
+            small[f"M{Ms}"] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (3 * len(weights)),
                                "frac_hbm": (nbytes / (ms * 1e-3) / 1e9) / pk["hbm_gbs"], "bytes_per_pass": nbytes,
                                "launches_per_pass": 3 * len(weights)}
             del g
@@ -299,60 +412,11 @@ def run_ours(args, world, rank, local):
     # --- M <= 16 on N > 1 GPUs: output-channel split of each GEMM (one all-gather of y) ---
     tp = None
     if world > 1 and not args.no_small:
-        import math
-        import torch.distributed as dist
-        from comfy_ui_gfx906_tools_b200 import parallel
-        full_bytes = sum(N * K // 2 + N * (K // 32) * 2 for (_, K, N) in SHAPES)
-        ncopy = max(3, math.ceil(3 * 126e6 * world / full_bytes))  # per-rank shards of all copies > 2x L2
-        shard_sets = []
-        for c in range(ncopy):
-            cp = weights if c == 0 else make_weights(dev, seed=5000 + 100 * c)
-            sh = []
-            for (_, K, N, p, s) in cp:
-                n0, n1 = parallel.channel_block(N, rank, world)
-                sh.append((K, N, p[n0:n1].contiguous(), s[n0:n1].contiguous()))
-            shard_sets.append(sh)
-            del cp
-        tp = {"copies": ncopy, "split": f"output channels / {world}, all_gather_into_tensor of y",
-              "fused": "w4a16_gemm_allgather (epilogue stores into every rank's symmetric-memory y) + peer barrier"}
-        sag = parallel.SymmetricAllGather(max(N for (_, _, N) in SHAPES), torch.bfloat16, dev)
-        for Ms in (1, 16):
-            xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev).to(torch.bfloat16).contiguous()
-                   for i, (_, K, _) in enumerate(SHAPES)]
-            outs = [torch.empty(world * Ms, N // world, dtype=torch.bfloat16, device=dev) for (_, _, N) in SHAPES]
-
-            def tp_pass():
-                for sh in shard_sets:
-                    for (K, N, p, s), x, o in zip(sh, xsm, outs):
-                        y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
-                        dist.all_gather_into_tensor(o, y)
-
-            def fused_pass():
-                for sh in shard_sets:
-                    for (K, N, p, s), x in zip(sh, xsm):
-                        sag.gemm(x, p, s, None, N // world)
-            reps = 5
-            nbytes = ncopy * sum(N * K // 2 + N * (K // 32) * 2 + Ms * K * 2 + Ms * N * 2 for (_, K, N) in SHAPES)
-            # the fused pass captured once in a CUDA graph (an even number of calls, so the
-            # y buffers keep alternating between replays): the host launches one graph
-            side = torch.cuda.Stream(dev)
-            side.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(side):
-                fused_pass()
-            torch.cuda.current_stream(dev).wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=side):
-                fused_pass()
-            for key, fn in ((f"M{Ms}", tp_pass), (f"M{Ms}_fused", fused_pass), (f"M{Ms}_fused_graph", graph.replay)):
-                ms = max_over_ranks(time_steps(fn, reps, 2, world, dev, stream) / reps, world, dev)
-                tp[key] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (ncopy * len(SHAPES)),
-                           "frac_hbm_aggregate": (nbytes / (ms * 1e-3) / 1e9) / (world * pk["hbm_gbs"])}
-            del graph
-        del shard_sets, sag
+        tp = run_channel_split(args, world, rank, dev, stream, weights, pk)
 
     # --- int8 weights (config 3): the six shapes at M=4608, per-channel fp16 scales ---
     int8 = None
-    if not args.no_int8:
+    if not args.no_int8 and world == 1:
         w8 = []
         for i, (name, K, N, _, _) in enumerate(weights):
             q, sc = synthetic.int8_weight(N, K, seed=5000 + i)
@@ -361,38 +425,40 @@ def run_ours(args, world, rank, local):
         def step8():
             for (q, sc), x in zip(w8, xs):
                 ops.gemm_w8a16(x, q, sc, None, torch.bfloat16)
-        ms8 = max_over_ranks(time_steps(step8, args.steps, args.warmup, world, dev, stream), world, dev)
-        ms8 /= args.steps
-        int8 = {"value": world * flops_step / (ms8 * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms8,
+        ms8 = time_steps(step8, args.steps, args.warmup, world, dev, stream) / args.steps
+        int8 = {"value": flops_step / (ms8 * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms8,
                 "weights": "int8 ~round(N(0,40)) clipped to +-127, one fp16 scale per output channel",
-                "frac_of_sustained_peak": (flops_step / (ms8 * 1e-3) / 1e12) / pk["bf16_tflops_sustained"]}
+                "frac_of_burst_peak": (flops_step / (ms8 * 1e-3) / 1e12) / pk["bf16_tflops"]}
         del w8
 
     # --- e2e: public API with host buffers, H2D of x and D2H of y inside the timed region ---
     # (pinned host buffers; the copies of one step overlap its GEMMs and each other)
     e2e = None
     if not args.no_e2e:
-        xh = [x.cpu().pin_memory() for x in xs]
-        yh = [torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for (_, K, N, _, _) in weights]
-        xd = [torch.empty_like(x) for x in xs]
-
+        xh = [x.cpu().pin_memory() for x in xloc]
+        yh = [torch.empty(M if world > 1 else per, N, dtype=torch.bfloat16).pin_memory()
+              for (_, K, N, _, _) in weights]
+        xd = [torch.empty_like(x) for x in xloc]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
         def e2e_step():
-            # host->device copies on s_in, GEMMs on the launching stream, device->host on
-            # s_out: copies of shape i+1 / i-1 overlap GEMM i and run in both PCIe directions
+            # host->device copies on s_in, GEMMs (and the all-gathers) on the launching
+            # stream, device->host on s_out: the copies of shape i+1 / i-1 overlap GEMM i
             s_in.wait_stream(stream)
             s_out.wait_stream(stream)
             landed = []
             with torch.cuda.stream(s_in):
                 for i in range(len(weights)):
                     xd[i].copy_(xh[i], non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(s_in)
-                    landed.append(ev)
+                    ev_ = torch.cuda.Event()
+                    ev_.record(s_in)
+                    landed.append(ev_)
             for i, (_, K, N, p, s) in enumerate(weights):
                 stream.wait_event(landed[i])
                 y = ops.gemm_w4a16(xd[i], p, s, None, torch.bfloat16)
+                if world > 1:
+                    dist.all_gather_into_tensor(yfull[i], y)
+                    y = yfull[i]
                 done = torch.cuda.Event()
                 done.record(stream)
                 s_out.wait_event(done)
@@ -400,42 +466,126 @@ def run_ours(args, world, rank, local):
                 with torch.cuda.stream(s_out):
                     yh[i].copy_(y, non_blocking=True)
             stream.wait_stream(s_out)  # the step ends when the last result is on the host
-        ms_e2e = max_over_ranks(time_steps(e2e_step, max(2, args.steps // 2), 2, world, dev, stream), world, dev)
-        ms_e2e /= max(2, args.steps // 2)
-        e2e = {"value": world * flops_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
-               "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs),
-               "d2h_bytes_per_step": sum(M * N * 2 for (_, K, N, _, _) in weights), "ms_per_step": ms_e2e}
+        n_e2e = max(2, args.steps // 2)
+        ms_e2e = max_over_ranks(time_steps(e2e_step, n_e2e, 2, world, dev, stream), world, dev) / n_e2e
+        e2e = {"value": flops_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": sum(x.numel() * 2 for x in xloc),
+               "d2h_bytes_per_step": sum(y.numel() * 2 for y in yh), "ms_per_step": ms_e2e}
+
+    # --- config 5 at N GPUs: the 2048^2 DiT forward, token rows split across the ranks ---
+    dit = None
+    if not args.no_dit:
+        dit = run_dit_rows(world, rank, dev, stream, steps=2, warmup=1)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cores = len(os.sched_getaffinity(0))
-        torch.set_num_threads(cores)
-        best = None
-        for _ in range(2):
-            t_dq, t_mm, f, s = cpu_reference_sample(0, 256)
-            best = s if best is None else min(best, s)
-        cpu = {"value": f / best / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": "qkv 3072x9216: torch-CPU dequant of the full weight + fp32 matmul of 256 of 4608 rows, "
-                         "extrapolated to M=4608 (t_dequant + 18*t_matmul), best of 2"}
+        cpu = cpu_baseline_best_of(3)
 
     if rank == 0:
+        peak = pk["bf16_tflops"]
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "flux_linear_sweep", "M": M, "shapes": [s[0] for s in SHAPES],
-                       "weights": "int4 group-32, ggml Q4_0 synthetic (fp16-exact scales)",
-                       "l2": "each step reads > 126 MB of distinct inputs (no flush needed)",
-                       "clock_soak_s": 1.0,
-                       "parallelism": f"replicas x{world} (per-GPU token block, no collective)"},
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_kind": f"bf16 dense sustained ({pk['source']})",
-                         "frac_of_burst": achieved / pk["bf16_tflops"], "traffic": traffic},
+                         "frac": achieved / peak,
+                         "peak_kind": f"bf16 dense burst ({pk['source']}): the 20-step timed loop is ~45 ms",
+                         "frac_of_sustained": achieved / pk["bf16_tflops_sustained"],
+                         "step_frac": (value / world) / peak, "traffic": traffic,
+                         "kernel": "wq_tc_kernel<1, bf16, 1> (tcgen05), mean over the six shapes' launches",
+                         "launch_ms": {weights[i][0]: launch_ms[i] / args.steps for i in range(len(weights))}},
+            "parity": {"ok": parity_ok, "rows_sampled": 64, "per_shape": parity,
+                       "reference": "torch fp32 dequant-then-matmul of the sampled rows (north-star tolerance "
+                                    "2e-2 max-abs ratio, 5e-3 mean relative error)"},
             "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8,
             **({"small_m_channel_split": tp} if tp is not None else {}),
+            **({"dit_rows": dit} if dit is not None else {}),
             "gpu_launches": args.steps * len(weights), "clocks": clocks.summary(),
         }
         print(json.dumps(out))
+
+
+def run_channel_split(args, world, rank, dev, stream, weights, pk):
+    """M in {1, 16} at N > 1: each rank streams N/G of every weight's rows;
+    GEMM + NCCL all-gather, and the fused kernel (peer stores + flag barrier)."""
+    import math
+    import torch.distributed as dist
+    from comfy_ui_gfx906_tools_b200 import ops, parallel, synthetic
+    full_bytes = sum(N * K // 2 + N * (K // 32) * 2 for (_, K, N) in SHAPES)
+    ncopy = max(3, math.ceil(3 * 126e6 * world / full_bytes))  # per-rank shards of all copies > 2x L2
+    shard_sets = []
+    for c in range(ncopy):
+        cp = weights if c == 0 else make_weights(dev, seed=5000 + 100 * c)
+        sh = []
+        for (_, K, N, p, s) in cp:
+            n0, n1 = parallel.channel_block(N, rank, world)
+            sh.append((K, N, p[n0:n1].contiguous(), s[n0:n1].contiguous()))
+        shard_sets.append(sh)
+        del cp
+    tp = {"copies": ncopy, "split": f"output channels / {world}, all_gather_into_tensor of y",
+          "fused": "w4a16_gemm_allgather (epilogue stores into every rank's symmetric-memory y) + peer barrier"}
+    sag = parallel.SymmetricAllGather(max(N for (_, _, N) in SHAPES), torch.bfloat16, dev)
+    for Ms in (1, 16):
+        xsm = [synthetic.activations(Ms, K, seed=4000 + i).to(dev).to(torch.bfloat16).contiguous()
+               for i, (_, K, _) in enumerate(SHAPES)]
+        outs = [torch.empty(world * Ms, N // world, dtype=torch.bfloat16, device=dev) for (_, _, N) in SHAPES]
+
+        def tp_pass():
+            for sh in shard_sets:
+                for (K, N, p, s), x, o in zip(sh, xsm, outs):
+                    y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+                    dist.all_gather_into_tensor(o, y)
+
+        def fused_pass():
+            for sh in shard_sets:
+                for (K, N, p, s), x in zip(sh, xsm):
+                    sag.gemm(x, p, s, None, N // world)
+        reps = 5
+        nbytes = ncopy * sum(N * K // 2 + N * (K // 32) * 2 + Ms * K * 2 + Ms * N * 2 for (_, K, N) in SHAPES)
+        # the fused pass captured once in a CUDA graph (an even number of calls, so the
+        # y buffers keep alternating between replays): the host launches one graph
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fused_pass()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            fused_pass()
+        for key, fn in ((f"M{Ms}", tp_pass), (f"M{Ms}_fused", fused_pass), (f"M{Ms}_fused_graph", graph.replay)):
+            ms = max_over_ranks(time_steps(fn, reps, 2, world, dev, stream) / reps, world, dev)
+            tp[key] = {"GB_s": nbytes / (ms * 1e-3) / 1e9, "us_per_gemm": 1e3 * ms / (ncopy * len(SHAPES)),
+                       "frac_hbm_aggregate": (nbytes / (ms * 1e-3) / 1e9) / (world * pk["hbm_gbs"])}
+        del graph
+    del shard_sets, sag
+    return tp
+
+
+def run_dit_rows(world, rank, dev, stream, steps, warmup, res=2048):
+    """Config 5: the full Flux-architecture DiT forward at res^2 (random int4
+    weights), token rows split across the ranks (one image-K/V all-gather per
+    attention); tokens/s over the ranks, max-over-ranks CUDA-event time."""
+    from comfy_ui_gfx906_tools_b200 import flux_dit, parallel
+    cfg = flux_dit.DiTConfig()
+    model = flux_dit.FluxDiT(cfg, flux_dit.int4_linear_factory(dev, seed=11), dev)  # same seed: identical replicas
+    side = res // 16
+    inputs = flux_dit.make_inputs(cfg, 1, side, side, 512, dev, seed=12)
+
+    def fwd():
+        with torch.no_grad():
+            if world > 1:
+                return parallel.split_forward_rows(model, *inputs, side, side, gather_output=False)
+            return model(*inputs)
+    ms = max_over_ranks(time_steps(fwd, steps, warmup, world, dev, stream), world, dev) / steps
+    tokens = side * side + 512
+    del model
+    torch.cuda.empty_cache()
+    return {"metric": "Flux DiT forward tokens/s (int4 linears)", "value": tokens / (ms * 1e-3), "unit": "tokens/s",
+            "ms_per_forward": ms, "steps": steps, "warmup": warmup,
+            "config": {"workload": f"flux_dit_{res}", "batch": 1, "image_tokens": side * side, "text_tokens": 512,
+                       "split": "token rows" if world > 1 else "none",
+                       "blocks": "19 double + 38 single, hidden 3072"}}
 
 
 def run_dit(args, world, rank, local):
@@ -483,28 +633,100 @@ def run_dit(args, world, rank, local):
         }))
 
 
+def run_case(args):
+    """One GEMM shape on cuda:0, timed with CUDA events (the command the ncu
+    summaries under profiles/ profile): synthetic Q4_0 weights used through
+    their fp16 scale copy as Gfx906Int4Ops.Linear does, activations bf16
+    N(0, 1); prints the time per GEMM, TFLOP/s and GB/s of algorithmic bytes
+    (N*K/2 + N*K/32*scale_bytes + 2*M*K + 2*M*N)."""
+    from comfy_ui_gfx906_tools_b200 import ops, synthetic
+    shapes = {name: (K, N) for name, K, N in SHAPES}
+    K, N = (args.k, args.n) if args.n and args.k else shapes[args.case]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ws = []
+    for c in range(args.copies):
+        raw, _, _ = synthetic.q4_0_weight(N, K, seed=10 + c)
+        p, s = ops.repack_q4_0_native(raw.to(dev), N, K)
+        if not args.fp32_scales:
+            s = ops.scales_to_f16_if_exact(s)
+        ws.append((p, s))
+    x = synthetic.activations(args.m, K, seed=1).to(dev)
+    stream = torch.cuda.Stream(dev)
+
+    def run():
+        for i in range(args.reps):
+            p, s = ws[i % args.copies]
+            if args.int8:
+                ops.gemm_w8a16(x, p8[i % args.copies][0], p8[i % args.copies][1], None, torch.bfloat16)
+            else:
+                ops.gemm_w4a16(x, p, s, None, torch.bfloat16, splits=args.splits)
+
+    p8 = [tuple(t.to(dev) for t in synthetic.int8_weight(N, K, seed=20 + c)) for c in range(args.copies)] \
+        if args.int8 else None
+    with torch.cuda.stream(stream):
+        run()  # warm-up (also creates this stream's split-K workspace)
+        torch.cuda.synchronize(dev)
+        fn = run
+        if args.graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+            fn = g.replay
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    us = 1e3 * e0.elapsed_time(e1) / args.reps
+    sb = 2 if args.int8 else ws[0][1].element_size()
+    wbytes = N * K if args.int8 else N * K // 2 + N * (K // 32) * sb
+    nbytes = wbytes + 2 * args.m * K + 2 * args.m * N
+    print(json.dumps({"case": args.case if not (args.n and args.k) else f"{N}x{K}", "M": args.m, "N": N, "K": K,
+                      "us": us, "tflops": 2 * args.m * N * K / us / 1e6, "GB_s": nbytes / us / 1e3,
+                      "graph": args.graph, "copies": args.copies, "splits": args.splits, "int8": args.int8}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--m", type=int, default=4608)
     ap.add_argument("--no-small", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-int8", action="store_true")
+    ap.add_argument("--no-dit", action="store_true")
     ap.add_argument("--workload", choices=["gemm", "dit"], default="gemm")
     ap.add_argument("--res", type=int, default=1024, help="dit: latent resolution in pixels (1024 or 2048)")
     ap.add_argument("--split", choices=["batch", "rows"], default="batch", help="dit: how N > 1 ranks split")
     ap.add_argument("--batch", type=int, default=0, help="dit: batch (default 8 for the batch split, else 1)")
+    ap.add_argument("--case", default=None, choices=[s[0] for s in SHAPES] + ["custom"],
+                    help="time one GEMM shape instead of the bench (with --m, --reps, --graph, --copies)")
+    ap.add_argument("--m", type=int, default=M_FULL)
+    ap.add_argument("--n", type=int, default=0, help="case custom: N (with --k)")
+    ap.add_argument("--k", type=int, default=0)
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--copies", type=int, default=1, help="case: distinct weight copies cycled through (defeats L2)")
+    ap.add_argument("--fp32-scales", action="store_true")
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--graph", action="store_true", help="case: time a CUDA graph of the reps")
+    ap.add_argument("--int8", action="store_true", help="case: the int8 (W8A16) kernel, per-channel scales")
     args = ap.parse_args()
+    if args.case is not None:
+        run_case(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, world, rank)
         return
-    world, rank, local = setup_dist(args.gpus)
+    world, rank, local = setup_dist()
+    if args.workload == "gemm" and M_FULL % world != 0:
+        raise SystemExit(f"--gpus {world} must divide M={M_FULL}")
     try:
         if args.workload == "dit":
             run_dit(args, world, rank, local)

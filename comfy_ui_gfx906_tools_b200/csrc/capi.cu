@@ -86,8 +86,122 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
 
 static bool valid_dtype(int d) { return d == GFX_DTYPE_F32 || d == GFX_DTYPE_F16 || d == GFX_DTYPE_BF16; }
 
-static int check_gemm_common(const char* fn, const void* x, int x_dtype, const void* w, const void* ws,
-                             int scale_dtype, void* y, int out_dtype, int M, int N, int K, int splits) {
+// ---------------------------------------------------------------------------
+// tensor-map cache: a model's weight maps are encoded once per (device, args)
+// ---------------------------------------------------------------------------
+namespace {
+struct TmapKey {
+  int dev;
+  int dtype;
+  const void* base;
+  uint64_t inner, outer, stride;
+  uint32_t box_inner, box_outer;
+  int swizzle;
+  bool operator==(const TmapKey& o) const {
+    return dev == o.dev && dtype == o.dtype && base == o.base && inner == o.inner && outer == o.outer &&
+           stride == o.stride && box_inner == o.box_inner && box_outer == o.box_outer && swizzle == o.swizzle;
+  }
+};
+constexpr int kTmapSlots = 512;  // direct-mapped by a hash of the key; a collision re-encodes
+struct TmapSlot {
+  bool valid = false;
+  TmapKey key{};
+  CUtensorMap map;
+};
+std::mutex g_tmap_mu;
+TmapSlot g_tmap[kTmapSlots];
+}  // namespace
+
+int cached_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  const TmapKey key{current_device(), (int)dtype, base, inner, outer, row_stride_bytes, box_inner, box_outer,
+                    (int)swizzle};
+  uint64_t h = reinterpret_cast<uintptr_t>(base) >> 4;
+  h ^= inner * 0x9E3779B97F4A7C15ull ^ outer * 0xC2B2AE3D27D4EB4Full ^ ((uint64_t)key.dev << 40) ^
+       ((uint64_t)box_inner << 20) ^ ((uint64_t)box_outer << 8) ^ (uint64_t)key.swizzle ^ ((uint64_t)dtype << 4);
+  h ^= h >> 29;
+  TmapSlot& slot = g_tmap[h % kTmapSlots];
+  {
+    std::lock_guard<std::mutex> lock(g_tmap_mu);
+    if (slot.valid && slot.key == key) {
+      *map = slot.map;
+      return GFX_OK;
+    }
+  }
+  int rc = make_tmap_2d(map, dtype, base, inner, outer, row_stride_bytes, box_inner, box_outer, swizzle);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  slot.valid = true;
+  slot.key = key;
+  slot.map = *map;
+  return GFX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// host-visible status words: one page of host memory, pinned and mapped into
+// every device's address space, one 64-byte slot per device
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kMaxDevices = 64;
+alignas(4096) int g_status_page[kMaxDevices * 16];
+std::once_flag g_status_once;
+bool g_status_mapped = false;
+unsigned g_fail_epoch[kMaxDevices] = {};
+std::mutex g_status_mu;
+}  // namespace
+
+int* host_status_word(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_status_once, [] {
+    g_status_mapped = cudaHostRegister(g_status_page, sizeof(g_status_page),
+                                       cudaHostRegisterPortable | cudaHostRegisterMapped) == cudaSuccess;
+    if (!g_status_mapped) (void)cudaGetLastError();
+  });
+  if (!g_status_mapped) return nullptr;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, g_status_page, 0) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  return reinterpret_cast<int*>(d) + dev * 16;
+}
+
+int host_status_read(int dev) {
+  if (dev < 0 || dev >= kMaxDevices || !g_status_mapped) return 0;
+  return *reinterpret_cast<volatile int*>(&g_status_page[dev * 16]);
+}
+
+void host_status_clear(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  volatile int* w = reinterpret_cast<volatile int*>(&g_status_page[dev * 16]);
+  if (*w != 0) {
+    *w = 0;
+    ++g_fail_epoch[dev];
+  }
+}
+
+unsigned failure_epoch(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  return g_fail_epoch[dev];
+}
+
+int check_device_health(const char* fn, int dev, void* workspace, size_t counter_bytes, cudaStream_t stream) {
+  const int v = host_status_read(dev);
+  if (v == 0) return GFX_OK;
+  bool rearmed = false;
+  if (workspace != nullptr && counter_bytes > 0)
+    rearmed = cudaMemsetAsync(workspace, 0, counter_bytes, stream) == cudaSuccess;
+  (void)cudaGetLastError();
+  return set_error(GFX_ERR_DEVICE,
+                   "%s: device %d reports status %d: an earlier kernel gave up in a bounded wait, so results "
+                   "computed since then are not valid%s; read and clear it with gfx_device_status(1)",
+                   fn, dev, v, rearmed ? " (the split-K counters of this call's workspace were re-zeroed)" : "");
+}
+
+int check_gemm_common(const char* fn, const void* x, int x_dtype, const void* w, const void* ws, int scale_dtype,
+                      void* y, int out_dtype, int M, int N, int K, int splits) {
   if (M < 0 || N <= 0 || K <= 0)
     return set_error(GFX_ERR_INVALID, "%s: expected M >= 0, N > 0, K > 0; got M=%d N=%d K=%d", fn, M, N, K);
   if (K % 32 != 0)
@@ -131,6 +245,10 @@ int gfx_device_status(int clear) {
     if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
     if (p && !v) v = p;
   }
+  const int dev = current_device();
+  const int h = host_status_read(dev);
+  if (h && !v) v = h;
+  if (clear) host_status_clear(dev);
   return v;
 }
 
@@ -152,8 +270,12 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
   int rc = check_gemm_common("w4a16_gemm", x, x_dtype, w_q4, w_scale, scale_dtype, y, out_dtype, M, N, K, splits);
   if (rc) return rc;
   if (M == 0) return GFX_OK;
-  const int sms = sm_count(current_device());
+  const int dev = current_device();
+  const int sms = sm_count(dev);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = check_device_health("w4a16_gemm", dev, workspace,
+                           workspace_bytes >= kSplitKCounterBytes ? kSplitKCounterBytes : 0, st);
+  if (rc) return rc;
   // M > 64 always runs on the tcgen05 kernel (its tiles cover K whole, so a
   // requested split count only matters for the small-M kernel, as for the
   // reference where `splits` changes speed, not the result's definition).
@@ -178,6 +300,10 @@ int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const voi
   if (M > 64)
     return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm_allgather: M <= 64 only (the HBM-bound case), got M=%d", M);
   if (M == 0) return GFX_OK;
+  rc = check_device_health("w4a16_gemm_allgather", current_device(), workspace,
+                           workspace_bytes >= kSplitKCounterBytes ? kSplitKCounterBytes : 0,
+                           reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
   gfx::OutTargets t{};
   for (int q = 0; q < n_ranks; ++q) t.ptr[q] = y_ranks[q];
   t.count = n_ranks;
@@ -210,6 +336,8 @@ int w8a16_gemm(const void* x, int x_dtype, const void* w_q8, const void* w_scale
   if (scale_per_channel && (reinterpret_cast<uintptr_t>(w_scale) & 1))
     return set_error(GFX_ERR_INVALID, "w8a16_gemm: float16 channel scales must be 2-byte aligned");
   if (M == 0) return GFX_OK;
+  rc = check_device_health("w8a16_gemm", current_device(), nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
   // Every M runs on the tensor-core kernel (the int8 path has no small-M kernel yet).
   return launch_w8a16_tc(x, w_q8, w_scale, scale_per_channel, bias, y, out_dtype, M, N, K,
                          reinterpret_cast<cudaStream_t>(stream), sm_count(current_device()));

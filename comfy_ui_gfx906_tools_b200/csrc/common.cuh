@@ -60,6 +60,20 @@ __device__ __forceinline__ void record_device_error(int code) {
   atomicCAS(&g_device_error, 0, code);
 }
 
+// Copy this translation unit's status word, if set, into `host_word`: one int
+// of pinned, mapped host memory per device (host_status_word below), so that
+// the host sees a wait that gave up before its next launch without a device
+// synchronisation. Called on the failure paths only; a null word (host memory
+// could not be mapped) skips it.
+__device__ __forceinline__ void mirror_device_error(int* host_word) {
+  if (host_word == nullptr) return;
+  const int v = *(volatile int*)&g_device_error;
+  if (v != 0) {
+    *(volatile int*)host_word = v;
+    __threadfence_system();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // shared-memory addresses and mbarriers
 // ---------------------------------------------------------------------------
@@ -303,4 +317,27 @@ int current_device();
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// Same, through a small per-device cache keyed on every argument: the weight
+// maps of a model's layers are encoded once, not on every call.
+int cached_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
+// Host-visible status word of `dev` (a device-usable pointer into pinned,
+// mapped host memory), or nullptr when that memory could not be mapped.
+int* host_status_word(int dev);
+// Its current value (a plain host read; no device synchronisation).
+int host_status_read(int dev);
+// Zero it; bumps the device's failure epoch when it was set.
+void host_status_clear(int dev);
+// Counts the failures cleared on `dev`; a cached scratch buffer whose split-K
+// counters were last re-zeroed at an older epoch must re-zero them again.
+unsigned failure_epoch(int dev);
+// GFX_OK, or GFX_ERR_DEVICE (with a message) when `dev` reports a wait that
+// gave up; then the first counter_bytes of `workspace` (the split-K arrival
+// counters, if any) are re-zeroed on `stream` before returning.
+int check_device_health(const char* fn, int dev, void* workspace, size_t counter_bytes, cudaStream_t stream);
+
+// Argument checks shared by the GEMM entry points (messages name `fn`).
+int check_gemm_common(const char* fn, const void* x, int x_dtype, const void* w, const void* ws, int scale_dtype,
+                      void* y, int out_dtype, int M, int N, int K, int splits);
 }  // namespace gfx

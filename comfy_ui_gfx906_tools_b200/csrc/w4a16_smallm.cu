@@ -86,6 +86,15 @@ constexpr int kConsumerBarrier = 1;             // named barrier id for the 256 
 #ifndef GFX_SMALLM_STAGES_NT2
 #define GFX_SMALLM_STAGES_NT2 4   // smem ring depth, fp16 scales, 8 < M <= 16
 #endif
+#ifndef GFX_SMALLM_GRID_NT1
+#define GFX_SMALLM_GRID_NT1 GFX_SMALLM_CTAS_PER_SM  // CTAs per SM in the grid plan, M <= 8
+#endif
+#ifndef GFX_SMALLM_GRID_NT2
+#define GFX_SMALLM_GRID_NT2 GFX_SMALLM_CTAS_NT2     // CTAs per SM in the grid plan, 8 < M <= 16
+#endif
+#ifndef GFX_SMALLM_PREWAIT
+#define GFX_SMALLM_PREWAIT 0  // 1: load the first stages' weights into the ring before the dependency wait
+#endif
 
 // Warp tiling: kMT m16 tiles per warp (rows), the 8 consumer warps split into
 // kRowSlices row slices x kKParts K parts (each K part owns kGPW of the 8
@@ -167,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     const __grid_constant__ CUtensorMap scale_map, int scale_tma, const void* __restrict__ wscale,
     const OutT* __restrict__ bias, OutT* __restrict__ y, const __grid_constant__ OutTargets out,
     float* __restrict__ partials,
-    int* __restrict__ counters,
+    int* __restrict__ counters, int* status_host,
     int M, int N, int K, int G, int max_segs) {
   using L = Layout<NT, STAGES, kF16Scale>;
   constexpr int kTok = L::kTok;
@@ -213,35 +222,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 
   if (warp == kConsumerWarps) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0) {
-      tma_prefetch_desc(&nib_map);
-      tma_prefetch_desc(&x_map);
-      if (scale_tma) tma_prefetch_desc(&scale_map);
-      // the first stages' weight tiles start streaming into L2 while the
-      // previous kernel of the stream finishes
-      const int pre = n_iters < STAGES ? n_iters : STAGES;
-      for (int it = 0; it < pre; ++it) {
-        const long long u = u_begin + it;
-        tma_prefetch_l2_2d(&nib_map, (int)(u % KS) * kStageBytesPerRow, (int)(u / KS) * kRows);
-      }
-    }
-    pdl_wait();
-    for (int it = 0; it < n_iters; ++it) {
+    // weights (nibbles + scales) of unit it into ring stage it % STAGES,
+    // counted on full[stage] together with the activation boxes
+    auto load_weights = [&](int it) {
       const int stage = it % STAGES;
-      const uint32_t phase = (it / STAGES) & 1;
-      if (!mbar_wait(&empty[stage], phase ^ 1, kDevErrEmptyBarrierTimeout)) break;
       const long long u = u_begin + it;
       const int rb = (int)(u / KS), ks = (int)(u % KS);
       uint8_t* st = smem + stage * L::kStageBytes;
       uint8_t* sc = st + L::kNibBytes;
-      uint8_t* xs = sc + L::kScaleBytes;
       if (lane == 0) {
         mbar_arrive_expect_tx(&full[stage],
                               L::kNibBytes + 4 * L::kXBoxBytes + (scale_tma ? kRows * L::kScaleRowBytes : 0));
         tma_load_2d(st, &nib_map, &full[stage], ks * kStageBytesPerRow, rb * kRows);
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tma_load_2d(xs + b * L::kXBoxBytes, &x_map, &full[stage], ks * kStageK + b * 64, tok0);
         if (scale_tma) tma_load_2d(sc, &scale_map, &full[stage], ks * kGroupsPerStage, rb * kRows);
       }
       if (!scale_tma) {
@@ -258,6 +250,49 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
         }
         cp_async_mbar_arrive_noinc(&full[stage]);
       }
+    };
+    // the activation slice of unit it (only after the dependency wait)
+    auto load_x = [&](int it) {
+      const int stage = it % STAGES;
+      const int ks = (int)((u_begin + it) % KS);
+      uint8_t* xs = smem + stage * L::kStageBytes + L::kNibBytes + L::kScaleBytes;
+      if (lane == 0) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          tma_load_2d(xs + b * L::kXBoxBytes, &x_map, &full[stage], ks * kStageK + b * 64, tok0);
+      }
+    };
+    const int pre = n_iters < STAGES ? n_iters : STAGES;
+    if (lane == 0) {
+      tma_prefetch_desc(&nib_map);
+      tma_prefetch_desc(&x_map);
+      if (scale_tma) tma_prefetch_desc(&scale_map);
+      if (!GFX_SMALLM_PREWAIT) {
+        // the first stages' weight tiles start streaming into L2 while the
+        // previous kernel of the stream finishes
+        for (int it = 0; it < pre; ++it) {
+          const long long u = u_begin + it;
+          tma_prefetch_l2_2d(&nib_map, (int)(u % KS) * kStageBytesPerRow, (int)(u / KS) * kRows);
+        }
+      }
+    }
+    // Weights never come from another kernel, so with GFX_SMALLM_PREWAIT the
+    // first `pre` stages' weights land in the ring while the previous kernel
+    // of the stream still runs; only the activation boxes wait for it.
+    if (GFX_SMALLM_PREWAIT)
+      for (int it = 0; it < pre; ++it) load_weights(it);  // first use of each stage: no empty wait
+    pdl_wait();
+    for (int it = 0; it < n_iters; ++it) {
+      if (!(GFX_SMALLM_PREWAIT && it < pre)) {
+        const int stage = it % STAGES;
+        const uint32_t phase = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[stage], phase ^ 1, kDevErrEmptyBarrierTimeout)) {
+          mirror_device_error(status_host);
+          break;
+        }
+        load_weights(it);
+      }
+      load_x(it);
     }
     if constexpr (kCl) cluster_sync_all();  // no CTA of the cluster leaves while a peer may address it
     return;
@@ -285,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     // A consumer that gives up here leaves early; its peers reach the same
     // wait (they all consume the same stages) and give up the same way.
     if (!mbar_wait(&full[stage], phase, kDevErrFullBarrierTimeout)) {
+      mirror_device_error(status_host);
       if constexpr (kCl) cluster_sync_all();
       return;
     }
@@ -461,7 +497,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
       const int vt = (M - tok0) < kTok ? (M - tok0) : kTok;  // valid tokens of this token block
       float* recv = reinterpret_cast<float*>(smem);
       if (rank != 0) {
-        if (kq == 0 && mbar_wait_acq_cluster(cl_go, 0, kDevErrClusterReduceTimeout)) {
+        if (kq == 0 && !mbar_wait_acq_cluster(cl_go, 0, kDevErrClusterReduceTimeout)) {
+          mirror_device_error(status_host);
+        } else if (kq == 0) {
           const uint32_t dst = mapa_shared(smem_u32(recv), 0) + (rank - 1) * (uint32_t)(kTok * kRecvStride * 4);
 #pragma unroll
           for (int mt = 0; mt < kMT; ++mt)
@@ -482,7 +520,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
         consumer_sync();  // every consumer is done reading the ring (K-part reduction)
         if (threadIdx.x == 0)
           for (uint32_t q = 1; q < csize; ++q) mbar_arrive_release_cluster(cl_go, q);
-        if (kq == 0 && mbar_wait_acq_cluster(cl_red, 0, kDevErrClusterReduceTimeout)) {
+        if (kq == 0 && !mbar_wait_acq_cluster(cl_red, 0, kDevErrClusterReduceTimeout)) {
+          mirror_device_error(status_host);
+        } else if (kq == 0) {
 #pragma unroll
           for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
@@ -606,7 +646,7 @@ static SmallMPlan smallm_plan(int M, int N, int K, int splits_req, int sms, bool
   p.RB = (N + smallm::kRows - 1) / smallm::kRows;
   p.KS = (K + smallm::kStageK - 1) / smallm::kStageK;
   // resident CTAs per SM follow the stage ring + reduction buffer size
-  p.ctas_per_sm = p.nt == 4 ? 1 : (p.nt == 2 ? GFX_SMALLM_CTAS_NT2 : GFX_SMALLM_CTAS_PER_SM);
+  p.ctas_per_sm = p.nt == 4 ? 1 : (p.nt == 2 ? GFX_SMALLM_GRID_NT2 : GFX_SMALLM_GRID_NT1);
   p.stages = p.nt == 4 ? 6 : ((!f16 && p.nt == 2) ? 3 : 4);
   const long long U = (long long)p.RB * p.KS;
   long long G;
@@ -668,6 +708,7 @@ struct SmallMArgs {
   OutTargets out;
   float* part;
   int* cnt;
+  int* status_host;
   int M, N, K;
 };
 
@@ -693,8 +734,8 @@ static int launch_smallm_k(const SmallMPlan& p, const SmallMArgs& a, cudaStream_
     cfg.numAttrs = 2;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.nib_map, a.x_map, a.scale_map, a.scale_tma, a.ws,
-                                     (const OutT*)a.bias, (OutT*)a.out.ptr[0], a.out, a.part, a.cnt, a.M, a.N, a.K,
-                                     p.G, p.max_segs);
+                                     (const OutT*)a.bias, (OutT*)a.out.ptr[0], a.out, a.part, a.cnt, a.status_host, a.M,
+                                     a.N, a.K, p.G, p.max_segs);
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a16_smallm_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a16_smallm_kernel");
 }
@@ -804,8 +845,9 @@ int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, i
   // calls of any shape sharing one workspace always find them re-armed to
   // zero; the fp32 partials follow and need no initial value.
   a.cnt = reinterpret_cast<int*>(workspace);
+  a.status_host = host_status_word(current_device());
   a.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kSplitKCounterBytes);
-  int rc = make_tmap_2d(&a.nib_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+  int rc = cached_tmap_2d(&a.nib_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                         smallm::kStageBytesPerRow, smallm::kRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&a.x_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
@@ -815,7 +857,7 @@ int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, i
   const uint64_t groups = (uint64_t)K / 32;
   a.scale_tma = ((groups * elem) % 16 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) ? 1 : 0;
   if (a.scale_tma) {
-    rc = make_tmap_2d(&a.scale_map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws,
+    rc = cached_tmap_2d(&a.scale_map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws,
                       groups, (uint64_t)N, groups * elem, smallm::kGroupsPerStage, smallm::kRows,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
@@ -855,7 +897,8 @@ struct FlagTable {
   int* p[kMaxOutTargets];
 };
 
-__global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int n_ranks, int rank) {
+__global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int n_ranks, int rank,
+                                    int* status_host) {
   const int q = threadIdx.x;
   int* own = flags.p[rank];
   const int epoch = own[n_ranks] + 1;
@@ -870,6 +913,7 @@ __global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int
       if (v - epoch >= 0) break;
       if (global_timer_ns() - t0 > kWaitTimeoutNs) {
         record_device_error(kDevErrPeerBarrierTimeout);
+        mirror_device_error(status_host);
         break;
       }
       __nanosleep(64);
@@ -882,7 +926,7 @@ __global__ void peer_barrier_kernel(const __grid_constant__ FlagTable flags, int
 int launch_peer_barrier(int* const* flags, int n_ranks, int rank, cudaStream_t stream) {
   FlagTable t{};
   for (int q = 0; q < n_ranks; ++q) t.p[q] = flags[q];
-  peer_barrier_kernel<<<1, 32, 0, stream>>>(t, n_ranks, rank);
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(t, n_ranks, rank, host_status_word(current_device()));
   return check_launch("peer_barrier_kernel");
 }
 

@@ -63,8 +63,12 @@ constexpr int kTileN = 128;       // weight rows per tile (MMA M)
 constexpr int kTileM = 256;       // tokens per tile (MMA N)
 constexpr int kStageK = 64;       // K per pipeline stage (one 128-byte swizzle row of bf16)
 constexpr int kUmmaK = 16;
-constexpr int kThreads = 14 * 32;
-constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6, kDequantWarps = 8;
+#ifndef GFX_TC_DEQ_WARPS
+#define GFX_TC_DEQ_WARPS 8
+#endif
+constexpr int kEpiWarps = 4, kProducerWarp = 4, kMmaWarp = 5, kDequantWarp0 = 6, kDequantWarps = GFX_TC_DEQ_WARPS;
+constexpr int kThreads = (kDequantWarp0 + kDequantWarps) * 32;
+static_assert(kDequantWarps == 8 || kDequantWarps == 16, "dequant warps: 8 or 16");
 #ifndef GFX_TC_DEQ_GROUPS
 #define GFX_TC_DEQ_GROUPS 2
 #endif
@@ -299,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
                                                             const __grid_constant__ CUtensorMap q_map,
                                                             const void* __restrict__ wscale,
                                                             const OutT* __restrict__ bias, OutT* __restrict__ y,
-                                                            int M, int N, int K) {
+                                                            int M, int N, int K, int* status_host) {
   using T = Traits<F, C>;
   constexpr int kStages = T::kStages;
   constexpr int kStageBytes = T::kStageBytes;
@@ -464,12 +468,18 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   } else if (warp >= kDequantWarp0) {
     // -------------------------------- dequant ---------------------------------
     // reads only shared memory the producer filled after its pdl_wait()
-    // The 8 warps form kG groups; group q dequantizes the stages with
+    // The dequant warps form kG groups; group q dequantizes the stages with
     // kit % kG == q, so kG stages are in flight at once. A stage holds 256
-    // items (128 rows x two 32-groups); each thread of a group takes kG of
-    // them: items tg, tg + 256/kG, ... (row = item % 128, group = item / 128).
+    // items (128 rows x two 32-groups); each thread of a group takes
+    // kItemsPerThread of them: items tg, tg + kGroupThreads, ... (row =
+    // item % 128, group = item / 128).
     constexpr int kGroupThreads = kDequantWarps * 32 / kG;
-    const int dt = (warp - kDequantWarp0) * 32 + lane;  // 0..255
+    // a stage holds 2 * kTileN items; a group wider than that leaves its
+    // extra threads idle (they still take part in the stage hand-off)
+    constexpr int kItemsPerThread = kGroupThreads >= 2 * kTileN ? 1 : 2 * kTileN / kGroupThreads;
+    static_assert(kGroupThreads >= 2 * kTileN ? kGroupThreads % (2 * kTileN) == 0
+                                              : kItemsPerThread * kGroupThreads == 2 * kTileN, "dequant item split");
+    const int dt = (warp - kDequantWarp0) * 32 + lane;
     const int q = dt / kGroupThreads, tg = dt % kGroupThreads;
     uint32_t kit = 0;
     for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
@@ -496,8 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
         }
         const uint8_t* sc = qt + T::kQBytes;
 #pragma unroll
-        for (int item_j = 0; item_j < kG; ++item_j) {
+        for (int item_j = 0; item_j < kItemsPerThread; ++item_j) {
           const int item = tg + item_j * kGroupThreads;
+          if (kGroupThreads > 2 * kTileN && item >= 2 * kTileN) break;
           const int g = item / kTileN;  // 32-wide half of the stage
           const int r = item % kTileN;  // weight row within the tile
           const uint32_t wrow = smem_u32(st + kXBytes) + r * 128;
@@ -599,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
       }
       __syncwarp();
     }
-    mbar_wait(sm.drain, 0, kDevErrMmaBarrierTimeout);
+    if (!mbar_wait(sm.drain, 0, kDevErrMmaBarrierTimeout)) ok = false;
   } else {
     // -------------------------------- epilogue --------------------------------
     pdl_wait();  // y, bias and channel scales are touched only after the previous kernel
@@ -642,6 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     }
   }
 
+  if (!ok) mirror_device_error(status_host);
   tc_fence_before();
   if constexpr (C == 2) {
     cluster_sync_all();  // no CTA leaves while its peer may still touch its barriers or smem
@@ -727,7 +739,8 @@ static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const void*
   const int tiles = ((N + rows - 1) / rows) * ((M + tc::kTileM - 1) / tc::kTileM);
   const int units = tiles < clusters ? tiles : clusters;
   cfg.gridDim = dim3(C * units);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K,
+                                     host_status_word(dev));
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "wq_tc_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("wq_tc_kernel");
 }
@@ -754,7 +767,7 @@ static int launch_tc_out(int out_dtype, const void* x, const CUtensorMap& qm, co
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
   CUtensorMap qm;
-  int rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+  int rc = cached_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                     tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   if (scale_dtype == GFX_SCALE_F16)
@@ -765,7 +778,7 @@ int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dty
 int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
   CUtensorMap qm;
-  int rc = make_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, tc::kStageK,
+  int rc = cached_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, tc::kStageK,
                     tc::kTileN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   if (per_channel) return launch_tc_out<tc::kInt8ChanF16>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);

@@ -17,6 +17,7 @@ the loader are plain functions here so they run without ComfyUI; the node
 methods import ComfyUI lazily. Packing and dequantization run as this
 package's GPU kernels (``ops``); results equal the reference's torch code.
 
+The multi-GPU split node (Gfx906RowSplitKrea2) lives in row_split.py.
 Out of scope (not the int4 DiT linear path): the CLIP transcode / loader
 nodes, the fused-attention node and the int8 VAE node of the reference.
 """
@@ -372,14 +373,18 @@ class Gfx906Int4UnetLoader:
         return (model_patcher,)
 
 
+from .row_split import Gfx906RowSplitKrea2  # noqa: E402  (the multi-GPU split node, row_split.py)
+
 NODE_CLASS_MAPPINGS = {
     "Gfx906Int4Patch": Gfx906Int4Patch,
     "Gfx906Int4UnetLoader": Gfx906Int4UnetLoader,
     "Gfx906Int4Transcode": Gfx906Int4Transcode,
+    "Gfx906RowSplitKrea2": Gfx906RowSplitKrea2,
 }
 
 NODE_DISPLAY_NAME_MAPPINGS = {
     "Gfx906Int4Transcode": "Gfx906 Int4 Transcode (native kernel, any source)",
     "Gfx906Int4Patch": "Gfx906 Int4 Quantize (test)",
     "Gfx906Int4UnetLoader": "Gfx906 Int4 UNet Loader (native kernel)",
+    "Gfx906RowSplitKrea2": "Gfx906 Split Krea2 (2 GPUs)",
 }

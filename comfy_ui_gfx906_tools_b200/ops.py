@@ -72,6 +72,42 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor |
         return ws
 
 
+def _rearm_workspaces(device: torch.device):
+    """Zero every cached split-K workspace of `device`: after a kernel gave up
+    in a bounded wait, its row blocks' arrival counters may be left non-zero,
+    and a later call sharing the workspace would sum the wrong segments."""
+    with _ws_lock:
+        for (idx, _), ws in _workspaces.items():
+            if idx == device.index:
+                ws.zero_()
+
+
+def device_status(device: torch.device | None = None, clear: bool = False) -> int:
+    """The device's status word (synchronises it): 0 when healthy, else the
+    code of the first bounded device-side wait that gave up (1-7, see
+    include/gfx906_b200.h). ``clear`` resets it and re-zeroes the cached
+    split-K workspaces, after which the GEMMs run again."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        v = int(_lib.load().gfx_device_status(1 if clear else 0))
+        if clear:
+            _rearm_workspaces(device)
+            torch.cuda.synchronize(device)
+    return v
+
+
+def _call_gemm(name: str, device: torch.device, *args):
+    """A GEMM entry point; a GFX_ERR_DEVICE (an earlier kernel gave up in a
+    bounded wait) also re-zeroes this device's cached workspaces before the
+    error propagates. The status stays set until ``device_status(clear=True)``."""
+    try:
+        _lib.call(name, *args)
+    except _lib.GfxError as e:
+        if e.code == _lib.GFX_ERR_DEVICE:
+            _rearm_workspaces(device)
+        raise
+
+
 # ---------------------------------------------------------------------------
 # Hadamard rotation helpers (reference ops.py:43-105), torch on the tensor's device
 # ---------------------------------------------------------------------------
@@ -144,14 +180,10 @@ def hadamard_rotate(x: torch.Tensor, group: int, out_dtype: torch.dtype = torch.
 
 
 def apply_group_rotation(t: torch.Tensor, R: torch.Tensor, group: int) -> torch.Tensor:
-    """Rotate every group-sized chunk of the last dim: flat @ R^T (ops.py:85-105)."""
+    """Rotate every group-sized chunk of the last dim: flat @ R^T (ops.py:85-105),
+    on t's own device."""
     shape = t.shape
-    flat = t.reshape(-1, group)
-    if flat.device.type == "cpu" and torch.cuda.is_available():
-        rotated = (flat.cuda() @ R.t().cuda()).to("cpu")
-    else:
-        rotated = flat @ R.t().to(flat.device)
-    return rotated.reshape(shape)
+    return (t.reshape(-1, group) @ R.t().to(t.device, t.dtype)).reshape(shape)
 
 
 # ---------------------------------------------------------------------------
@@ -326,7 +358,7 @@ def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, b
         L = _lib.load()
         nbytes = int(L.w4a16_workspace_bytes(M, N, K, splits))
         ws = _workspace(dev, stream, nbytes)
-        _lib.call("w4a16_gemm", xb.data_ptr(), _lib.DTYPE_BF16, Bp.data_ptr(), Bs.data_ptr(),
+        _call_gemm("w4a16_gemm", dev, xb.data_ptr(), _lib.DTYPE_BF16, Bp.data_ptr(), Bs.data_ptr(),
                   _lib.SCALE_F16 if Bs.dtype == torch.float16 else _lib.SCALE_F32, bias_ptr, out.data_ptr(),
                   _dtype_code(out_dtype), M, N, K, splits, ws.data_ptr() if ws is not None else None,
                   ws.numel() if ws is not None else 0, stream)
@@ -370,8 +402,8 @@ def gemm_w8a16(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor, bias: to
     xb = (x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)).contiguous()
     Bc, Bs = B.contiguous(), B_scale.contiguous()
     with torch.cuda.device(x.device):
-        _lib.call("w8a16_gemm", xb.data_ptr(), _lib.DTYPE_BF16, Bc.data_ptr(), Bs.data_ptr(), per_channel, bias_ptr,
-                  out.data_ptr(), _dtype_code(out_dtype), M, N, K, 0, None, 0, _stream(x.device))
+        _call_gemm("w8a16_gemm", x.device, xb.data_ptr(), _lib.DTYPE_BF16, Bc.data_ptr(), Bs.data_ptr(), per_channel,
+                   bias_ptr, out.data_ptr(), _dtype_code(out_dtype), M, N, K, 0, None, 0, _stream(x.device))
     return out
 
 

@@ -149,11 +149,17 @@ class SymmetricAllGather:
     The barrier keeps its epoch on the device, so a sequence of calls can be
     captured in a CUDA graph; capture an even number of calls, so that the
     buffers keep alternating from one replay to the next.
+
+    A peer that never reaches the barrier makes it give up after 2 s and
+    record status 7: the next GEMM call on this device then raises GfxError
+    (code GFX_ERR_DEVICE) before it launches anything; ``strict=True`` also
+    synchronises after every barrier and raises at once.
     """
 
     ROWS = 64  # the small-M kernel's limit
 
-    def __init__(self, n_max: int, dtype: torch.dtype, device: torch.device, group=None):
+    def __init__(self, n_max: int, dtype: torch.dtype, device: torch.device, group=None, strict: bool = False):
+        self.strict = strict
         import torch.distributed._symmetric_memory as symm_mem
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
@@ -190,12 +196,17 @@ class SymmetricAllGather:
             stream = torch.cuda.current_stream(self.device).cuda_stream
             L = _lib.load()
             ws = ops._workspace(self.device, stream, int(L.w4a16_workspace_bytes(M, n_local, K, 0)))
-            _lib.call("w4a16_gemm_allgather", xb.data_ptr(), _lib.DTYPE_BF16, w_q4.data_ptr(), scale.data_ptr(),
+            ops._call_gemm("w4a16_gemm_allgather", self.device, xb.data_ptr(), _lib.DTYPE_BF16, w_q4.data_ptr(), scale.data_ptr(),
                       _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32,
                       bias.data_ptr() if bias is not None else None, self._targets[parity], self.world,
                       self.rank, ops._dtype_code(self.dtype), M, n_local, K, 0,
                       ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
             _lib.call("gfx_peer_barrier", self._flag_ptr, self.world, self.rank, stream)
+            status = ops.device_status(self.device) if self.strict else 0
+            if status != 0:
+                raise _lib.GfxError("gfx_peer_barrier", _lib.GFX_ERR_DEVICE,
+                                    f"device status {status} after the fused all-gather (a peer did not reach "
+                                    "the barrier within its 2 s budget)")
         return self.ybuf[parity, :M * n_total].view(M, n_total)
 
 

@@ -319,23 +319,25 @@ def test_gemm_config1_single_linear_full(cuda):
 
 @pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
 def test_gemm_flux_shapes_m4608_full_size(cuda, name, K, N):
-    """The Flux linear sweep (config 2) at full size. The oracle checks 96 sampled token rows
-    exactly (all N outputs each) and every row through a size-independent
-    checksum: sum_n Y[m, n] == X[m] . sum_n W[n] (linearity), in fp64."""
+    """The Flux linear sweep (config 2) at full size, every row: the fp32
+    output against the oracle of the kernel's exact operands (bf16(code *
+    scale), fp32 accumulation) at 1e-5, the bf16 output against the fp32
+    dequant-then-matmul at the north-star bar, and every row through a
+    size-independent checksum: sum_n Y[m, n] == X[m] . sum_n W[n] (linearity),
+    in fp64."""
     M = 4608
     p, s, pd, sd = _weights(N, K, seed=K * 3 + N, dev=cuda)
     sd16 = ops.scales_to_f16_if_exact(sd)
     x = synthetic.activations(M, K, seed=77)
+    xn = x.float().numpy()
+    y32 = ops.gemm_w4a16(x.to(cuda), pd, sd16, None, torch.float32).cpu().numpy()
+    _check(y32, O.w4a16_matmul_bf16w(xn, p, s), 1e-5, 1e-5)
     y = ops.gemm_w4a16(x.to(cuda), pd, sd16, None, torch.bfloat16).float()
-    rows = np.random.default_rng(0).choice(M, 96, replace=False)
-    xs = x[rows].float().numpy()
-    got = y[torch.from_numpy(rows).to(cuda)].cpu().numpy()
-    _check(got, O.w4a16_matmul(xs, p, s))
-    _check(got, O.w4a16_matmul_bf16w(xs, p, s), 8e-3, 2.5e-3)  # bf16 output rounding only
+    _check(y.cpu().numpy(), O.w4a16_matmul(xn, p, s))
     wsum = O.round_to_bf16(O.dequant_int4(p, s)).astype(np.float64).sum(axis=0)   # [K]
-    want = x.float().numpy().astype(np.float64) @ wsum                             # [M]
+    want = xn.astype(np.float64) @ wsum                                            # [M]
     gotsum = y.double().sum(dim=1).cpu().numpy()
-    scale = np.abs(x.float().numpy()).astype(np.float64) @ np.abs(wsum)
+    scale = np.abs(xn).astype(np.float64) @ np.abs(wsum)
     assert np.max(np.abs(gotsum - want) / (scale + 1e-30)) < 2e-3
 
 
@@ -359,19 +361,32 @@ def test_gemm_int8_block_scales(cuda, M, N, K):
     _check(y, ref)
 
 
-@pytest.mark.parametrize("M", [64, 4608])
-def test_gemm_int8_channel_scales_flux(cuda, M):
-    # config 3: int8 ~round(N(0,40)) clipped, one fp16 scale per output channel
-    K, N = 3072, 3072
-    q, s = synthetic.int8_weight(N, K, seed=5)
-    x = synthetic.activations(M, K, seed=6)
-    y = ops.gemm_w8a16(x.to(cuda), q.to(cuda), s.to(cuda), None, torch.bfloat16).float()
+@pytest.mark.parametrize("name,K,N", synthetic.FLUX_SHAPES)
+@pytest.mark.parametrize("M", [1, 16, 4608])
+def test_gemm_int8_channel_scales_flux(cuda, name, K, N, M):
+    """Config 3 at every Flux shape: int8 ~round(N(0,40)) clipped, one fp16
+    scale per output channel, against the reference's int8 dequant + fp32
+    matmul (bench_int8.py:32-43 restated by oracle.w8a16_matmul, with the
+    channel scale replicated to the [N, K/32] block layout). M=4608 checks 96
+    sampled rows exactly and every row through the linearity checksum."""
+    q, s = synthetic.int8_weight(N, K, seed=5 + K + N)
+    x = synthetic.activations(M, K, seed=6 + M)
+    xd, qd, sdd = x.to(cuda), q.to(cuda), s.to(cuda)
+    y = ops.gemm_w8a16(xd, qd, sdd, None, torch.bfloat16).float()
+    y32 = ops.gemm_w8a16(xd, qd, sdd, None, torch.float32)
     s_blk = np.repeat(s.float().numpy()[:, None], K // 32, axis=1)
-    rows = np.arange(M) if M <= 64 else np.random.default_rng(1).choice(M, 64, replace=False)
+    rows = np.arange(M) if M <= 64 else np.random.default_rng(1).choice(M, 96, replace=False)
+    rows_d = torch.from_numpy(rows).to(cuda)
     ref = O.w8a16_matmul(x[rows].float().numpy(), q.numpy(), s_blk)
-    _check(y[torch.from_numpy(rows).to(cuda)].cpu().numpy(), ref)
-    y32 = ops.gemm_w8a16(x.to(cuda), q.to(cuda), s.to(cuda), None, torch.float32)
-    _check(y32[torch.from_numpy(rows).to(cuda)].cpu().numpy(), ref, 1e-5, 1e-5)  # exact codes, fp32 scale
+    _check(y[rows_d].cpu().numpy(), ref)
+    _check(y32[rows_d].cpu().numpy(), ref, 1e-5, 1e-5)  # exact codes, fp32 channel scale
+    if M > 64:
+        wsum = (q.double() * s.double()[:, None]).sum(dim=0).numpy()                # [K]
+        xn = x.double().numpy()
+        want = xn @ wsum
+        scale = np.abs(xn) @ np.abs(wsum)
+        gotsum = y32.double().sum(dim=1).cpu().numpy()
+        assert np.max(np.abs(gotsum - want) / (scale + 1e-30)) < 1e-4
 
 
 def test_quantize_int4_activation_semantics(cuda):
