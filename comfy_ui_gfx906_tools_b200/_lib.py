@@ -54,6 +54,10 @@ SIGNATURES = {
     "quantize_int8": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int64, _c_int, _c_void_p]),
     "repack_q4_0": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "int4_dequant": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p]),
+    "int4_dequant_qblock": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_int,
+                                     _c_void_p]),
+    "w4a16_gemm_qblock": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
+                                   _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p]),
     "scales_to_f16": (_c_int, [_c_void_p, _c_void_p, _c_int64, _c_void_p, _c_void_p]),
 }
 

@@ -285,6 +285,30 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
                              workspace_bytes, st, sms);
 }
 
+int w4a16_gemm_qblock(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype, int qblock,
+                      const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+                      size_t workspace_bytes, gfx_stream_t stream) {
+  if (qblock == 32)
+    return w4a16_gemm(x, x_dtype, w_q4, w_scale, scale_dtype, bias, y, out_dtype, M, N, K, splits, workspace,
+                      workspace_bytes, stream);
+  if (qblock != 16)
+    return set_error(GFX_ERR_INVALID, "w4a16_gemm_qblock: qblock must be 32 or 16, got %d", qblock);
+  int rc = check_gemm_common("w4a16_gemm_qblock", x, x_dtype, w_q4, w_scale, scale_dtype, y, out_dtype, M, N, K,
+                             splits);
+  if (rc) return rc;
+  if (scale_dtype != GFX_SCALE_F32)
+    return set_error(GFX_ERR_UNSUPPORTED, "w4a16_gemm_qblock: qblock=16 takes float32 scales [N, K/16], got scale "
+                     "dtype %d", scale_dtype);
+  if (M == 0) return GFX_OK;
+  const int dev = current_device();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = check_device_health("w4a16_gemm_qblock", dev, nullptr, 0, st);
+  if (rc) return rc;
+  // 16-element groups run on the tensor-core kernel for every M (the
+  // reference's qblock=16 GEMMs are its training GEMMs, large M)
+  return launch_w4a16_tc(x, w_q4, w_scale, GFX_SCALE_F32, bias, y, out_dtype, M, N, K, st, sm_count(dev), 16);
+}
+
 int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
                          const void* bias, void* const* y_ranks, int n_ranks, int rank, int out_dtype, int M,
                          int N_local, int K, int splits, void* workspace, size_t workspace_bytes,
@@ -384,6 +408,23 @@ int repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, in
   if ((reinterpret_cast<uintptr_t>(packed) & 15) || (reinterpret_cast<uintptr_t>(raw) & 1))
     return set_error(GFX_ERR_INVALID, "repack_q4_0: packed must be 16-byte and raw 2-byte aligned");
   return launch_repack_q4_0(raw, packed, scale, scale_f16, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int int4_dequant_qblock(const void* w_q4, const void* w_scale, int scale_dtype, int qblock, void* out, int out_dtype,
+                        int N, int K, gfx_stream_t stream) {
+  if (qblock != 32 && qblock != 16)
+    return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: qblock must be 32 or 16, got %d", qblock);
+  if (N < 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: expected N >= 0 and K %% 32 == 0, got N=%d K=%d", N, K);
+  if (!valid_dtype(out_dtype)) return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: bad out dtype code %d", out_dtype);
+  if (scale_dtype != GFX_SCALE_F32 && scale_dtype != GFX_SCALE_F16)
+    return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: scale dtype must be 0 or 1, got %d", scale_dtype);
+  if (N == 0) return GFX_OK;
+  if (!w_q4 || !w_scale || !out) return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: null pointer");
+  if ((reinterpret_cast<uintptr_t>(w_q4) & 3) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return set_error(GFX_ERR_INVALID, "int4_dequant_qblock: weights must be 4-byte and out 16-byte aligned");
+  return launch_int4_dequant(w_q4, w_scale, scale_dtype, out, out_dtype, N, K, reinterpret_cast<cudaStream_t>(stream),
+                             qblock);
 }
 
 int int4_dequant(const void* w_q4, const void* w_scale, int scale_dtype, void* out, int out_dtype, int N, int K,

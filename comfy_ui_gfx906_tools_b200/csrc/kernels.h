@@ -44,8 +44,9 @@ int smallm_auto_splits(int M, int N, int K, int sms);
 int smallm_device_status(int clear);
 
 // W4A16 / W8A16, large M (tcgen05 + TMEM, persistent) -- w4a16_tc.cu
+// qblock 32 (fp32 or fp16 scales [N, K/32]) or 16 (fp32 scales [N, K/16]; any M)
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
-                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms, int qblock = 32);
 bool w4a16_tc_supported(int M, int N, int K, int scale_dtype);
 int tc_device_status(int clear);
 int selftest_device_status(int clear);
@@ -54,7 +55,7 @@ int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_chann
 
 // loaders / helpers -- pack.cu
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
-                        cudaStream_t stream);
+                        cudaStream_t stream, int qblock = 32);
 int launch_repack_q4_0(const void* raw, void* packed, float* scale, void* scale_f16, int N, int K,
                        cudaStream_t stream);
 int launch_quantize_pack_int4(const void* x, int x_dtype, void* packed, float* scale, int64_t rows, int K,

@@ -27,11 +27,11 @@ namespace gfx {
 // ---------------------------------------------------------------------------
 template <bool kF16Scale, typename OutT>
 __global__ void int4_dequant_kernel(const uint32_t* __restrict__ wq, const void* __restrict__ ws,
-                                    OutT* __restrict__ out, int64_t words, int groups_per_row) {
+                                    OutT* __restrict__ out, int64_t words, int words_per_group_log2) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= words) return;
   const uint32_t w = wq[i];
-  const int64_t grp = i >> 2;  // 4 words per 32-group; rows are whole groups
+  const int64_t grp = i >> words_per_group_log2;  // 4 words per 32-group, 2 per 16-group; rows are whole groups
   const float s = kF16Scale ? __half2float(reinterpret_cast<const __half*>(ws)[grp])
                             : reinterpret_cast<const float*>(ws)[grp];
   OutT v[8];
@@ -51,18 +51,18 @@ __global__ void int4_dequant_kernel(const uint32_t* __restrict__ wq, const void*
     for (int e = 0; e < 8; ++e) h[e] = *reinterpret_cast<uint16_t*>(&v[e]);
     *reinterpret_cast<uint4*>(dst) = packed;
   }
-  (void)groups_per_row;
 }
 
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, int qblock) {
   const int64_t words = (int64_t)N * K / 8;
   if (words == 0) return GFX_OK;
   const int threads = 256;
   const unsigned blocks = (unsigned)((words + threads - 1) / threads);
   const bool f16s = scale_dtype == GFX_SCALE_F16;
 #define DQ(F16S, T) \
-  int4_dequant_kernel<F16S, T><<<blocks, threads, 0, stream>>>((const uint32_t*)wq, ws, (T*)out, words, K / 32)
+  int4_dequant_kernel<F16S, T><<<blocks, threads, 0, stream>>>((const uint32_t*)wq, ws, (T*)out, words, \
+                                                                 qblock == 16 ? 1 : 2)
   if (out_dtype == GFX_DTYPE_F32) { if (f16s) DQ(true, float); else DQ(false, float); }
   else if (out_dtype == GFX_DTYPE_F16) { if (f16s) DQ(true, __half); else DQ(false, __half); }
   else { if (f16s) DQ(true, __nv_bfloat16); else DQ(false, __nv_bfloat16); }

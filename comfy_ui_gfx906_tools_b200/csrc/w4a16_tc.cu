@@ -20,8 +20,13 @@
 //   weight element feed 256 tokens, which halves the dequant work per FLOP
 //   compared with a 128-token tile.
 //   warp 4      TMA producer: x tile (TMA, 32 KB), packed weight tile (TMA:
-//               int4 4 KB SWIZZLE_32B, int8 8 KB SWIZZLE_64B) and per-group
-//               scales (cp.async) per 64-wide K stage.
+//               int4 4 KB SWIZZLE_32B, int8 8 KB SWIZZLE_64B) per 64-wide K
+//               stage, and the group scales of 4 stages at a time (one TMA
+//               box of 8 groups x 128 rows into one of two chunk buffers;
+//               per-stage cp.async when the scale rows are not 16-byte
+//               aligned). Gathering a row's 4 scale bytes per stage with
+//               cp.async measured as half of all shared-memory wavefronts,
+//               most of them bank conflicts.
 //   warps 6-13  dequant: each thread turns 32 weights of one row into bf16 in
 //               the UMMA canonical SW128 layout, then a proxy fence and an
 //               mbarrier arrival hand the stage to the MMA.
@@ -45,10 +50,13 @@
 // in fp32 and one rounding to bf16 equals the reference's two roundings; it is
 // computed as fma.rn.bf16x2(code, s_hi, code * s_lo) with s = s_hi + s_lo split
 // into two bf16 parts (code * s_lo is exact in bf16), 2.5 ops per element.
-// General fp32 scales use an fp32 multiply then one cvt.rn to bf16. int8 codes
-// are exact in bf16; a per-channel scale is applied to the fp32 accumulator.
+// General fp32 scales use an fp32 multiply then one cvt.rn to bf16; with
+// 16-element groups (the reference's qblock=16) each half of a 32-element
+// item takes its own scale. int8 codes are exact in bf16; a per-channel scale
+// is applied to the fp32 accumulator.
 // Every mbarrier wait is bounded (common.cuh).
 #include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -75,14 +83,10 @@ static_assert(kDequantWarps == 8 || kDequantWarps == 16, "dequant warps: 8 or 16
 // Dequant warp groups working on different stages at once (1, 2, 4 or 8).
 constexpr int kDeqGroups = GFX_TC_DEQ_GROUPS;
 static_assert(kDeqGroups == 1 || kDeqGroups == 2 || kDeqGroups == 4 || kDeqGroups == 8, "bad dequant grouping");
-#ifndef GFX_TC_SPLIT_NIB
-#define GFX_TC_SPLIT_NIB 0
-#endif
-constexpr uint32_t kNibLead = 4;  // stages the nibble ring runs ahead of the x tiles
 constexpr int kAccCols = kTileM;  // fp32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kWBytes = kTileN * kStageK * 2;  // 16 KB
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 320;
 constexpr int kSmemLimit = 232448;  // 227 KB per CTA
 
 // Weight formats.
@@ -91,33 +95,34 @@ enum Fmt : int {
   kInt4GroupF16 = 1,  // int4 nibbles, fp16-valued scale per 32-group (exact fp16 copy)
   kInt8GroupF32 = 2,  // int8, fp32 scale per 32-group (the reference's quantize_int8 format)
   kInt8ChanF16 = 3,   // int8, fp16 scale per output channel
+  kInt4Group16F32 = 4,  // int4 nibbles, fp32 scale per 16-group (the reference's qblock=16 format)
 };
 
 template <int F, int C>
 struct Traits {
   static constexpr int kXRows = kTileM / C;                    // tokens this CTA loads per stage
   static constexpr int kXBytes = kXRows * kStageK * 2;         // 32 KB, or 16 KB per CTA of a pair
-  static constexpr bool kInt8 = F >= kInt8GroupF32;
+  static constexpr bool kInt8 = F == kInt8GroupF32 || F == kInt8ChanF16;
+  static constexpr bool kG16 = F == kInt4Group16F32;  // four 16-groups per 64-wide K stage
   static constexpr bool kChannel = F == kInt8ChanF16;
   static constexpr bool kF16Group = F == kInt4GroupF16;
   static constexpr int kQRowBytes = kInt8 ? kStageK : kStageK / 2;  // packed bytes per row per stage
   static constexpr int kQBytes = kTileN * kQRowBytes;
-  static constexpr int kScaleBytes = kChannel ? 0 : 1024;            // 128 rows x 2 groups x <= 4 B
-  // int4 on one CTA: the packed weights and scales have a ring of their own
-  // (kNibSlots slots, loaded up to kNibLead stages ahead of the x tiles), so
-  // the dequant of a stage waits for its nibbles and a free weight slot only,
-  // never for the 32 KB x tile; the x TMA and the dequant then overlap instead
-  // of running one after the other in each ring slot. Off by default: on B200
-  // it measured ~20% slower (772 vs 963-972 TFLOP/s over the six Flux shapes
-  // at M = 4608; every parity test passes with it on).
-  static constexpr bool kSplit = C == 1 && !kInt8 && GFX_TC_SPLIT_NIB != 0;
-  static constexpr int kNibSlotBytes = kQBytes + kScaleBytes;         // 5 KB for int4
-  static constexpr int kNibSlots = kSplit ? 6 : 0;
-  static constexpr int kStageBytes = kXBytes + kWBytes + (kSplit ? 0 : kQBytes + kScaleBytes);
-  static constexpr int kFit = (kSmemLimit - 1024 - kBarrierBytes - kNibSlots * kNibSlotBytes) / kStageBytes;
-  static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNibSlots * kNibSlotBytes + kBarrierBytes;
-  static_assert(kNibSlotBytes % 1024 == 0, "nibble slots must stay 1024-byte aligned");
+  static constexpr int kGroupsPerStage = kChannel ? 0 : (kG16 ? 4 : 2);
+  static constexpr int kScaleElem = kF16Group ? 2 : 4;
+  // per-stage scale area of the cp.async path, [row][group]
+  static constexpr int kScaleBytes = kChannel ? 0 : (kTileN * kGroupsPerStage * kScaleElem + 1023) / 1024 * 1024;
+  // TMA path: one 2-D box of 8 groups x 128 rows ("a chunk", [row][8 groups],
+  // 16 B of fp16 or 32 B of fp32 per row) covers the scales of kChunkStages
+  // consecutive stages; two chunk buffers alternate.
+  static constexpr int kChunkGroups = 8;
+  static constexpr int kChunkStages = kChannel ? 1 : kChunkGroups / kGroupsPerStage;
+  static constexpr int kChunkRowBytes = kChunkGroups * kScaleElem;
+  static constexpr int kChunkBytes = kChannel ? 0 : kTileN * kChunkRowBytes;
+  static constexpr int kStageBytes = kXBytes + kWBytes + kQBytes + kScaleBytes;
+  static constexpr int kFit = (kSmemLimit - 1024 - kBarrierBytes - 2 * kChunkBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 6 ? 6 : kFit;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kChunkBytes + kBarrierBytes;
   static_assert(kStageBytes % 1024 == 0, "stage bases must stay 1024-byte aligned");
   static_assert(kStages >= 3, "pipeline too shallow");
 };
@@ -286,21 +291,22 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 
 struct Smem {
   uint8_t* stage0;     // stage s starts at stage0 + s * kStageBytes
-  uint64_t* full;      // [kStages] TMA + cp.async landed
+  uint8_t* chunk0;     // scale chunk b starts at chunk0 + b * kChunkBytes
+  uint64_t* full;      // [kStages] TMA (+ cp.async scales) landed
   uint64_t* wready;    // [kStages] dequantized weights written
   uint64_t* empty;     // [kStages] MMAs done reading the stage
   uint64_t* acc_full;  // [2]
   uint64_t* acc_empty; // [2]
   uint64_t* drain;     // [1]
-  uint8_t* nib0;       // split ring: slot n starts at nib0 + n * kNibSlotBytes
-  uint64_t* nfull;     // [kNibSlots] nibbles + scales landed
-  uint64_t* nempty;    // [kNibSlots] the dequant is done reading the slot
+  uint64_t* sfull;     // [2] scale chunk landed
+  uint64_t* sempty;    // [2] every dequant warp is done with the chunk
   uint32_t* tmem_base;
 };
 
 template <int F, typename OutT, int C>
 __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constant__ CUtensorMap x_map,
                                                             const __grid_constant__ CUtensorMap q_map,
+                                                            const __grid_constant__ CUtensorMap s_map, int scale_tma,
                                                             const void* __restrict__ wscale,
                                                             const OutT* __restrict__ bias, OutT* __restrict__ y,
                                                             int M, int N, int K, int* status_host) {
@@ -313,23 +319,24 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   // full[s] is exact only if the load kStages iterations earlier (the same
   // group's previous item on that stage) has already landed.
   constexpr int kG = kStages % kDeqGroups == 0 ? kDeqGroups : (kStages % 2 == 0 ? 2 : 1);
-  static_assert(!T::kSplit || T::kNibSlots % kG == 0, "a dequant group must own fixed nibble slots");
+  constexpr int kCS = T::kChunkStages;
+  static_assert(T::kChannel || kCS % kG == 0, "every dequant group must touch every scale chunk");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Smem sm;
   sm.stage0 = base;
-  sm.nib0 = base + kStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.nib0 + T::kNibSlots * T::kNibSlotBytes);
+  sm.chunk0 = base + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.chunk0 + 2 * T::kChunkBytes);
   sm.full = bars;
   sm.wready = bars + kStages;
   sm.empty = bars + 2 * kStages;
   sm.acc_full = bars + 3 * kStages;
   sm.acc_empty = bars + 3 * kStages + 2;
   sm.drain = bars + 3 * kStages + 4;
-  sm.nfull = bars + 3 * kStages + 5;
-  sm.nempty = sm.nfull + T::kNibSlots;
-  sm.tmem_base = reinterpret_cast<uint32_t*>(sm.nempty + T::kNibSlots);
-  static_assert((3 * kStages + 5 + 2 * T::kNibSlots) * 8 + 4 <= kBarrierBytes, "barrier area");
+  sm.sfull = bars + 3 * kStages + 5;
+  sm.sempty = bars + 3 * kStages + 7;
+  sm.tmem_base = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 9);
+  static_assert((3 * kStages + 9) * 8 + 4 <= kBarrierBytes, "barrier area");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -340,23 +347,22 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   const int num_tiles = tiles_n * tiles_m;
   const int first_tile = blockIdx.x / C, tile_step = gridDim.x / C;
   const int k_stages = (K + kStageK - 1) / kStageK;
-  const int groups = K >> 5;
+  const int groups = T::kG16 ? K >> 4 : K >> 5;
+  const bool stma = !T::kChannel && scale_tma != 0;  // host: aligned strides and k_stages % kCS == 0
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], (T::kChannel || T::kSplit) ? 1 : 1 + 32);
+      mbar_init(&sm.full[s], (T::kChannel || stma) ? 1 : 1 + 32);
       mbar_init(&sm.wready[s], kDequantWarps / kG * C);  // one group; a pair's arrive on CTA 0
       mbar_init(&sm.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm.acc_full[a], 1);
       mbar_init(&sm.acc_empty[a], kEpiWarps * C);
+      mbar_init(&sm.sfull[a], 1);
+      mbar_init(&sm.sempty[a], kDequantWarps);
     }
     mbar_init(sm.drain, 1);
-    for (int n = 0; n < T::kNibSlots; ++n) {
-      mbar_init(&sm.nfull[n], 1 + 32);
-      mbar_init(&sm.nempty[n], kDequantWarps / kG);
-    }
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<C>(sm.tmem_base, kTmemCols);
@@ -376,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     if (lane == 0) {
       tma_prefetch_desc(&x_map);
       tma_prefetch_desc(&q_map);
+      if (stma) tma_prefetch_desc(&s_map);
       // the first tile's first weight stages stream into L2 while the previous
       // kernel of the stream finishes
       if (first_tile < num_tiles) {
@@ -385,83 +392,50 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
       }
     }
     pdl_wait();
-    // per-row group scales of K stage ks for rows n0.. into sc (cp.async), then
-    // one no-increment arrival of this thread on bar when they have landed
-    auto load_scales = [&](uint8_t* sc, int n0, int ks, uint64_t* bar) {
-      if constexpr (!T::kChannel) {
-        const int g0 = ks * 2;
-        if constexpr (T::kF16Group) {
-          // one 4-byte word = the two fp16 scales of a row; smem layout [row]
-#pragma unroll
-          for (int j = 0; j < kTileN / 32; ++j) {
-            const int r = lane + 32 * j, n = n0 + r;
-            const bool valid = n < N && g0 < groups;
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-            if (valid) src += ((size_t)n * groups + g0) * 2;
-            cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
+    uint32_t kit = 0;
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
+      const int m0 = (tile / tiles_n) * kTileM + (int)cr * T::kXRows;
+      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        const int s = kit % kStages;
+        const uint32_t ph = (kit / kStages) & 1;
+        if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+        if (stma && kit % kCS == 0) {
+          // the scales of stages kit .. kit + kCS - 1 (one tile: k_stages % kCS == 0)
+          const uint32_t c = kit / kCS;
+          const int b = c & 1;
+          if (!mbar_wait(&sm.sempty[b], ((c >> 1) & 1) ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&sm.sfull[b], T::kChunkBytes);
+            tma_load_2d(sm.chunk0 + b * T::kChunkBytes, &s_map, &sm.sfull[b], ks * T::kGroupsPerStage, n0);
           }
-        } else {
-          // fp32, smem layout [group][row] (conflict-free reads)
+        }
+        uint8_t* st = sm.stage0 + s * kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
+          tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
+          tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
+        }
+        if (!T::kChannel && !stma) {
+          // cp.async fallback: this stage's scales into its [row][group] area,
+          // then one no-increment arrival per lane when they have landed
+          uint8_t* sc = st + kXBytes + kWBytes + T::kQBytes;
+          constexpr int kGS = T::kGroupsPerStage;
+          const int g0 = ks * kGS;
 #pragma unroll
-          for (int j = 0; j < 2 * kTileN / 32; ++j) {
-            const int i = lane + 32 * j, g = i / kTileN, r = i % kTileN, n = n0 + r;
+          for (int j = 0; j < kGS * kTileN / 32; ++j) {
+            const int i = lane + 32 * j, r = i % kTileN, g = i / kTileN, n = n0 + r;
             const bool valid = n < N && (g0 + g) < groups;
             const uint8_t* src = reinterpret_cast<const uint8_t*>(wscale);
-            if (valid) src += ((size_t)n * groups + g0 + g) * 4;
-            cp_async_4(sc + 4 * (g * kTileN + r), src, valid ? 4u : 0u);
+            if (valid) src += ((size_t)n * groups + g0 + g) * T::kScaleElem;
+            if constexpr (T::kScaleElem == 4) {
+              cp_async_4(sc + 4 * (r * kGS + g), src, valid ? 4u : 0u);
+            } else if (g == 0) {
+              // fp16: the two scales of a row are one aligned 4-byte word (K % 64 == 0)
+              cp_async_4(sc + 4 * r, src, valid ? 4u : 0u);
+            }
           }
-        }
-        cp_async_mbar_arrive_noinc(bar);
-      }
-    };
-    if constexpr (T::kSplit) {
-      // stage kit of this CTA = K stage kit % k_stages of its (kit / k_stages)-th tile
-      const int my_tiles = first_tile < num_tiles ? (num_tiles - first_tile + tile_step - 1) / tile_step : 0;
-      const uint32_t total = (uint32_t)my_tiles * (uint32_t)k_stages;
-      uint32_t nk = 0;
-      for (uint32_t kit = 0; kit < total && ok; ++kit) {
-        for (; nk < total && nk <= kit + kNibLead; ++nk) {
-          const int n = nk % T::kNibSlots;
-          if (!mbar_wait(&sm.nempty[n], ((nk / T::kNibSlots) & 1) ^ 1, kDevErrEmptyBarrierTimeout)) {
-            ok = false;
-            break;
-          }
-          const int tile = first_tile + (int)(nk / k_stages) * tile_step;
-          const int ks = nk % k_stages;
-          const int n0 = (tile % tiles_n) * kTileN;
-          uint8_t* qs = sm.nib0 + n * T::kNibSlotBytes;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&sm.nfull[n], T::kQBytes);
-            tma_load_2d(qs, &q_map, &sm.nfull[n], ks * T::kQRowBytes, n0);
-          }
-          load_scales(qs + T::kQBytes, n0, ks, &sm.nfull[n]);
-        }
-        if (!ok) break;
-        const int s = kit % kStages;
-        if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
-        const int tile = first_tile + (int)(kit / k_stages) * tile_step;
-        const int m0 = (tile / tiles_n) * kTileM;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full[s], kXBytes);
-          tma_load_2d(sm.stage0 + s * kStageBytes, &x_map, &sm.full[s], (int)(kit % k_stages) * kStageK, m0);
-        }
-      }
-    } else {
-      uint32_t kit = 0;
-      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
-        const int n0 = (tile % tiles_n) * kPairRows + (int)cr * kTileN;
-        const int m0 = (tile / tiles_n) * kTileM + (int)cr * T::kXRows;
-        for (int ks = 0; ks < k_stages; ++ks, ++kit) {
-          const int s = kit % kStages;
-          const uint32_t ph = (kit / kStages) & 1;
-          if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
-          uint8_t* st = sm.stage0 + s * kStageBytes;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
-            tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
-            tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
-          }
-          load_scales(st + kXBytes + kWBytes + T::kQBytes, n0, ks, &sm.full[s]);
+          cp_async_mbar_arrive_noinc(&sm.full[s]);
         }
       }
     }
@@ -470,17 +444,18 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     // reads only shared memory the producer filled after its pdl_wait()
     // The dequant warps form kG groups; group q dequantizes the stages with
     // kit % kG == q, so kG stages are in flight at once. A stage holds 256
-    // items (128 rows x two 32-groups); each thread of a group takes
-    // kItemsPerThread of them: items tg, tg + kGroupThreads, ... (row =
-    // item % 128, group = item / 128).
+    // items (128 rows x two 32-element halves of the 64-wide stage). A warp
+    // takes 16 rows x both halves per round: lane l -> row 16 b + (l & 7) +
+    // 8 (l >> 4), half (l >> 3) & 1. Then the 8 lanes of each quarter-warp
+    // store 8 different rows and the two quarters of each half-warp store
+    // different halves of the same 8 rows, so every 16-byte store of a
+    // half-warp lands on a distinct bank group of the 128-byte swizzle atom.
     constexpr int kGroupThreads = kDequantWarps * 32 / kG;
-    // a stage holds 2 * kTileN items; a group wider than that leaves its
-    // extra threads idle (they still take part in the stage hand-off)
-    constexpr int kItemsPerThread = kGroupThreads >= 2 * kTileN ? 1 : 2 * kTileN / kGroupThreads;
-    static_assert(kGroupThreads >= 2 * kTileN ? kGroupThreads % (2 * kTileN) == 0
-                                              : kItemsPerThread * kGroupThreads == 2 * kTileN, "dequant item split");
+    constexpr int kWarpsPerGroup = kGroupThreads / 32;
+    constexpr int kRounds = (kTileN / 16 + kWarpsPerGroup - 1) / kWarpsPerGroup;  // 16-row blocks per warp
     const int dt = (warp - kDequantWarp0) * 32 + lane;
-    const int q = dt / kGroupThreads, tg = dt % kGroupThreads;
+    const int q = dt / kGroupThreads, wg = (dt % kGroupThreads) >> 5;
+    const int r_in = (lane & 7) + 8 * (lane >> 4), g = (lane >> 3) & 1;
     uint32_t kit = 0;
     for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
       for (int ks = 0; ks < k_stages; ++ks, ++kit) {
@@ -488,38 +463,43 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
         uint8_t* st = sm.stage0 + s * kStageBytes;
-        const uint8_t* qt;
-        int nslot = 0;
-        if constexpr (T::kSplit) {
-          // its nibbles and scales have landed, and the MMAs that read this
-          // stage's weight slot kStages stages ago are done
-          nslot = kit % T::kNibSlots;
-          if (!mbar_wait(&sm.nfull[nslot], (kit / T::kNibSlots) & 1, kDevErrFullBarrierTimeout) ||
-              !mbar_wait(&sm.empty[s], ph ^ 1, kDevErrMmaBarrierTimeout)) {
-            ok = false;
-            break;
-          }
-          qt = sm.nib0 + nslot * T::kNibSlotBytes;
+        if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
+        const uint8_t* qt = st + kXBytes + kWBytes;
+        // scale of (row r, group gg of this stage): a chunk [row][8 groups] or
+        // the stage's own [row][group] area
+        const uint8_t* sbase;
+        int srow_bytes, sgroup0;
+        uint32_t c = 0;
+        if (stma) {
+          c = kit / kCS;
+          if (!mbar_wait(&sm.sfull[c & 1], (c >> 1) & 1, kDevErrFullBarrierTimeout)) { ok = false; break; }
+          sbase = sm.chunk0 + (c & 1) * T::kChunkBytes;
+          srow_bytes = T::kChunkRowBytes;
+          sgroup0 = (int)(kit % kCS) * T::kGroupsPerStage;
         } else {
-          if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
-          qt = st + kXBytes + kWBytes;
+          sbase = qt + T::kQBytes;
+          srow_bytes = T::kGroupsPerStage * T::kScaleElem;
+          sgroup0 = 0;
         }
-        const uint8_t* sc = qt + T::kQBytes;
 #pragma unroll
-        for (int item_j = 0; item_j < kItemsPerThread; ++item_j) {
-          const int item = tg + item_j * kGroupThreads;
-          if (kGroupThreads > 2 * kTileN && item >= 2 * kTileN) break;
-          const int g = item / kTileN;  // 32-wide half of the stage
-          const int r = item % kTileN;  // weight row within the tile
+        for (int rd = 0; rd < kRounds; ++rd) {
+          const int blk = rd * kWarpsPerGroup + wg;
+          if (kTileN / 16 % kWarpsPerGroup != 0 && blk >= kTileN / 16) break;
+          const int r = blk * 16 + r_in;  // weight row within the tile
           const uint32_t wrow = smem_u32(st + kXBytes) + r * 128;
           const int c0 = 4 * g, sw = r & 7;
+          const uint8_t* srow = sbase + r * srow_bytes;
           if constexpr (!T::kInt8) {
             // SWIZZLE_32B nibble tile: 16-byte half h of row r sits at half h ^ ((r >> 2) & 1)
             const uint4 qw = lds128(smem_u32(qt) + r * 32 + ((g ^ ((r >> 2) & 1)) << 4));
-            float sf;
+            float sf, sf1;
             uint32_t s_hi2 = 0, s_lo2 = 0;
-            if constexpr (T::kF16Group) {
-              sf = __half2float(reinterpret_cast<const __half*>(sc)[2 * r + g]);
+            if constexpr (T::kG16) {
+              // words 0-1 of the 32-element half are 16-group 2g, words 2-3 group 2g+1
+              sf = reinterpret_cast<const float*>(srow)[sgroup0 + 2 * g];
+              sf1 = reinterpret_cast<const float*>(srow)[sgroup0 + 2 * g + 1];
+            } else if constexpr (T::kF16Group) {
+              sf = __half2float(reinterpret_cast<const __half*>(srow)[sgroup0 + g]);
               const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
               const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
               const uint32_t hb = __float_as_uint(hi) >> 16;
@@ -527,16 +507,17 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
               s_hi2 = hb | (hb << 16);
               s_lo2 = lb | (lb << 16);
             } else {
-              sf = reinterpret_cast<const float*>(sc)[g * kTileN + r];
+              sf = reinterpret_cast<const float*>(srow)[sgroup0 + g];
             }
+            if constexpr (!T::kG16) sf1 = sf;
             constexpr bool kF16 = T::kF16Group;
             sts128(wrow + (((c0 + 0) ^ sw) << 4), dequant_nibble_word<kF16>(qw.x, sf, s_hi2, s_lo2));
             sts128(wrow + (((c0 + 1) ^ sw) << 4), dequant_nibble_word<kF16>(qw.y, sf, s_hi2, s_lo2));
-            sts128(wrow + (((c0 + 2) ^ sw) << 4), dequant_nibble_word<kF16>(qw.z, sf, s_hi2, s_lo2));
-            sts128(wrow + (((c0 + 3) ^ sw) << 4), dequant_nibble_word<kF16>(qw.w, sf, s_hi2, s_lo2));
+            sts128(wrow + (((c0 + 2) ^ sw) << 4), dequant_nibble_word<kF16>(qw.z, sf1, s_hi2, s_lo2));
+            sts128(wrow + (((c0 + 3) ^ sw) << 4), dequant_nibble_word<kF16>(qw.w, sf1, s_hi2, s_lo2));
           } else {
             // SWIZZLE_64B int8 tile (64-byte rows): chunk c of row r sits at c ^ ((r >> 1) & 3)
-            const float sf = T::kChannel ? 1.0f : reinterpret_cast<const float*>(sc)[g * kTileN + r];
+            const float sf = T::kChannel ? 1.0f : reinterpret_cast<const float*>(srow)[sgroup0 + g];
             const int xr = (r >> 1) & 3;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -554,10 +535,11 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
           // this CTA's x slice and dequantized rows of stage s are in place
           if constexpr (C == 1) {
             mbar_arrive(&sm.wready[s]);
-            if constexpr (T::kSplit) mbar_arrive(&sm.nempty[nslot]);  // the nibble slot may be refilled
           } else {
             mbar_arrive_cluster(&sm.wready[s], 0);
           }
+          // this warp's last stage of the scale chunk: the producer may refill it
+          if (stma && (int)(kit % kCS) >= kCS - kG) mbar_arrive(&sm.sempty[c & 1]);
         }
       }
     }
@@ -689,8 +671,8 @@ static int tc_ctas(int M) {
 }
 
 template <int F, typename OutT, int C>
-static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const void* ws, const void* bias, void* y, int M,
-                       int N, int K, cudaStream_t st, int sms) {
+static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const CUtensorMap& sm_map, int scale_tma,
+                       const void* ws, const void* bias, void* y, int M, int N, int K, cudaStream_t st, int sms) {
   using T = tc::Traits<F, C>;
   auto kern = tc::wq_tc_kernel<F, OutT, C>;
   static bool attr_set[64] = {false};
@@ -739,7 +721,7 @@ static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const void*
   const int tiles = ((N + rows - 1) / rows) * ((M + tc::kTileM - 1) / tc::kTileM);
   const int units = tiles < clusters ? tiles : clusters;
   cfg.gridDim = dim3(C * units);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, ws, (const OutT*)bias, (OutT*)y, M, N, K,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, sm_map, scale_tma, ws, (const OutT*)bias, (OutT*)y, M, N, K,
                                      host_status_word(dev));
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "wq_tc_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("wq_tc_kernel");
@@ -754,22 +736,46 @@ static int launch_tc_out(int out_dtype, const void* x, const CUtensorMap& qm, co
   int rc = make_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
                         tc::kStageK, tc::kTileM / C, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (C == 2) {
-    if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
-    if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
-    return launch_tc_t<F, __nv_bfloat16, 2>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  // Scales by TMA, one box of 8 groups x 128 rows per chunk of stages, when
+  // the scale rows are 16-byte aligned and no chunk crosses a tile's K end;
+  // otherwise per-stage cp.async.
+  using T1 = tc::Traits<F, 1>;
+  CUtensorMap sm_map;
+  memset(&sm_map, 0, sizeof(sm_map));
+  int scale_tma = 0;
+  if constexpr (!T1::kChannel) {
+    const uint64_t groups = (uint64_t)K / (T1::kG16 ? 16 : 32);
+    const int k_stages = (K + tc::kStageK - 1) / tc::kStageK;
+    if ((groups * T1::kScaleElem) % 16 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0 &&
+        k_stages % T1::kChunkStages == 0) {
+      rc = cached_tmap_2d(&sm_map, T1::kScaleElem == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          ws, groups, (uint64_t)N, groups * T1::kScaleElem, T1::kChunkGroups, tc::kTileN,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      scale_tma = 1;
+    }
   }
-  if (out_dtype == GFX_DTYPE_F32) return launch_tc_t<F, float, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
-  if (out_dtype == GFX_DTYPE_F16) return launch_tc_t<F, __half, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
-  return launch_tc_t<F, __nv_bfloat16, 1>(xm, qm, ws, bias, y, M, N, K, st, sms);
+  if (C == 2) {
+    if (out_dtype == GFX_DTYPE_F32)
+      return launch_tc_t<F, float, 2>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
+    if (out_dtype == GFX_DTYPE_F16)
+      return launch_tc_t<F, __half, 2>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
+    return launch_tc_t<F, __nv_bfloat16, 2>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
+  }
+  if (out_dtype == GFX_DTYPE_F32)
+    return launch_tc_t<F, float, 1>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
+  if (out_dtype == GFX_DTYPE_F16)
+    return launch_tc_t<F, __half, 1>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
+  return launch_tc_t<F, __nv_bfloat16, 1>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms);
 }
 
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
-                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
+                    int out_dtype, int M, int N, int K, cudaStream_t stream, int sms, int qblock) {
   CUtensorMap qm;
   int rc = cached_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                     tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
+  if (qblock == 16) return launch_tc_out<tc::kInt4Group16F32>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
   if (scale_dtype == GFX_SCALE_F16)
     return launch_tc_out<tc::kInt4GroupF16>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
   return launch_tc_out<tc::kInt4GroupF32>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);

@@ -272,21 +272,27 @@ def repack_q8_0(raw_bytes: torch.Tensor, out_features: int, in_features: int, bl
     return q, scale
 
 
-def dequantize_int4(w_packed: torch.Tensor, w_scale: torch.Tensor, out_dtype: torch.dtype = torch.float32):
+def dequantize_int4(w_packed: torch.Tensor, w_scale: torch.Tensor, out_dtype: torch.dtype = torch.float32,
+                    block: int = BLOCK):
     """Dequantize native int4 weights on the GPU: code * scale as one fp32
     multiply, rounded once to out_dtype (int4_train_test.py:46-52; bf16 out
-    = nodes.py:51-52 for a bf16 model)."""
+    = nodes.py:51-52 for a bf16 model). ``block`` is the scale block: 32
+    (scales [N, K/32]) or 16 (scales [N, K/16], the reference's qblock=16)."""
     _require_cuda(w_packed, "w_packed")
     N, half_k = w_packed.shape
     K = half_k * 2
     scale_code = _lib.SCALE_F16 if w_scale.dtype == torch.float16 else _lib.SCALE_F32
     if w_scale.dtype not in (torch.float16, torch.float32):
         raise RuntimeError(f"scales must be float32 or float16, got {w_scale.dtype}")
+    if block not in (32, 16):
+        raise RuntimeError(f"block must be 32 or 16, got {block}")
+    if w_scale.numel() != N * (K // block):
+        raise RuntimeError(f"scales must be [N, K/{block}] = {N * (K // block)} elements, got {w_scale.numel()}")
     wp, ws = w_packed.contiguous(), w_scale.contiguous()
     out = torch.empty(N, K, dtype=out_dtype, device=w_packed.device)
     with torch.cuda.device(w_packed.device):
-        _lib.call("int4_dequant", wp.data_ptr(), ws.data_ptr(), scale_code, out.data_ptr(), _dtype_code(out_dtype), N,
-                  K, _stream(w_packed.device))
+        _lib.call("int4_dequant_qblock", wp.data_ptr(), ws.data_ptr(), scale_code, block, out.data_ptr(),
+                  _dtype_code(out_dtype), N, K, _stream(w_packed.device))
     return out
 
 
@@ -312,13 +318,15 @@ def gemm_int4_auto_splits(M: int, N: int, K: int) -> int:
 
 
 def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, bias: torch.Tensor | None,
-               out_dtype: torch.dtype, splits: int = 0) -> torch.Tensor:
+               out_dtype: torch.dtype, splits: int = 0, qblock: int = 32) -> torch.Tensor:
     """C[M, N] = x[M, K] @ dequant(B_packed, B_scale)^T (+ bias), fp32 accumulate.
 
     x: bf16 [M, K] (other float dtypes are converted to bf16 first).
     B_packed int8 [N, K/2]; B_scale float32 (reference format) or float16
-    [N, K/32]; bias [N] in out_dtype or None. Argument checks and messages
-    follow gemm_int4 (binding.cpp:76-101).
+    [N, K/32]; with ``qblock=16`` float32 [N, K/16] (one scale per 16
+    elements, gemm_int4's qblock, int4_gemm_scaled.hip:153-160); bias [N] in
+    out_dtype or None. Argument checks and messages follow gemm_int4
+    (binding.cpp:76-101).
     """
     if not (x.is_cuda and B_packed.is_cuda):
         raise RuntimeError("inputs must be on device")
@@ -334,8 +342,12 @@ def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, b
         raise RuntimeError(f"expected K % 32 == 0, got K={K}")
     if B_scale.dtype not in (torch.float32, torch.float16):
         raise RuntimeError(f"scales must be float32 (or float16), got {B_scale.dtype}")
-    if B_scale.numel() != N * (K // 32):
-        raise RuntimeError(f"scales must be [N, K/32] = {N * (K // 32)} elements, got {B_scale.numel()}")
+    if qblock not in (32, 16):
+        raise RuntimeError(f"qblock must be 32 or 16, got {qblock}")
+    if qblock == 16 and B_scale.dtype != torch.float32:
+        raise RuntimeError(f"qblock=16 takes float32 scales, got {B_scale.dtype}")
+    if B_scale.numel() != N * (K // qblock):
+        raise RuntimeError(f"scales must be [N, K/{qblock}] = {N * (K // qblock)} elements, got {B_scale.numel()}")
     if not (0 <= splits <= 16):
         raise RuntimeError(f"splits must be in [0, 16], got {splits}")
     out = torch.empty(M, N, dtype=out_dtype, device=x.device)
@@ -355,6 +367,11 @@ def gemm_w4a16(x: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor, b
     dev = x.device
     with torch.cuda.device(dev):
         stream = _stream(dev)
+        if qblock == 16:  # the tensor-core kernel for every M; no workspace
+            _call_gemm("w4a16_gemm_qblock", dev, xb.data_ptr(), _lib.DTYPE_BF16, Bp.data_ptr(), Bs.data_ptr(),
+                       _lib.SCALE_F32, 16, bias_ptr, out.data_ptr(), _dtype_code(out_dtype), M, N, K, splits, None, 0,
+                       stream)
+            return out
         L = _lib.load()
         nbytes = int(L.w4a16_workspace_bytes(M, N, K, splits))
         ws = _workspace(dev, stream, nbytes)
@@ -457,8 +474,8 @@ def gemm_int4(A_packed: torch.Tensor, A_scale: torch.Tensor, B_packed: torch.Ten
     The A codes are dequantized exactly to bf16 (one rounding of code * scale)
     and multiplied on the W4A16 kernels; the result matches the reference's
     integer-block GEMM within bf16 rounding. qblock=16
-    (16-element scale blocks) is not supported by these kernels (their weight
-    groups are 32 elements) and raises."""
+    (16-element scale blocks, scales [M, K/16] / [N, K/16]) dequantizes A per
+    16-group and runs the tensor-core kernel's 16-group weight format."""
     if not (A_packed.is_cuda and B_packed.is_cuda):
         raise RuntimeError("inputs must be on device")
     if A_packed.device != B_packed.device:
@@ -477,14 +494,13 @@ def gemm_int4(A_packed: torch.Tensor, A_scale: torch.Tensor, B_packed: torch.Ten
     if A_scale.numel() != M * K // qblock or B_scale.numel() != N * K // qblock:
         raise RuntimeError(f"scales must be [M, K/{qblock}] / [N, K/{qblock}] = {M * K // qblock} / "
                            f"{N * K // qblock} elements, got {A_scale.numel()} / {B_scale.numel()}")
-    if qblock != 32:
-        raise RuntimeError("qblock=16 is not supported by the B200 kernels (32-element weight groups)")
     if splits < 0 or splits > 16:
         raise RuntimeError(f"splits must be in [0, 16], got {splits}")
     if M == 0:
         return torch.empty(0, N, dtype=out_dtype, device=A_packed.device)
-    xa = dequantize_int4(A_packed.contiguous(), A_scale.reshape(M, K // 32).contiguous(), torch.bfloat16)
-    return gemm_w4a16(xa, B_packed, B_scale.reshape(N, K // 32), bias, out_dtype, splits=splits)
+    xa = dequantize_int4(A_packed.contiguous(), A_scale.reshape(M, K // qblock).contiguous(), torch.bfloat16,
+                         block=qblock)
+    return gemm_w4a16(xa, B_packed, B_scale.reshape(N, K // qblock), bias, out_dtype, splits=splits, qblock=qblock)
 
 
 def gemm_int8(A: torch.Tensor, A_scale: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,

@@ -115,6 +115,18 @@ int w4a16_gemm(const void* x, int x_dtype, const void* w_q4, const void* w_scale
                size_t workspace_bytes, gfx_stream_t stream);
 
 /*
+ * W4A16 GEMM with a choice of scale block (gemm_int4's `qblock`,
+ * binding.cpp:73-112 / int4_gemm_scaled.hip:153-160, SUB = 2 for qblock 16).
+ * qblock 32: exactly w4a16_gemm. qblock 16: w_scale is float32 [N, K/16] (one
+ * scale per 16 elements, the reference's training format, train_linear.py:
+ * 45-67), any M, no workspace; each weight becomes bf16(code * scale) of its
+ * own 16-group. Other arguments as w4a16_gemm.
+ */
+int w4a16_gemm_qblock(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype, int qblock,
+                      const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+                      size_t workspace_bytes, gfx_stream_t stream);
+
+/*
  * W4A16 GEMM that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a plugin host that passes
  * only its input/output device pointers and owns the memory budget, or code
@@ -193,6 +205,12 @@ int repack_q8_0(const void* raw, void* q, float* scale, int N, int K, gfx_stream
  * operand the W4A16 tensor-core kernel multiplies with. */
 int int4_dequant(const void* w_q4, const void* w_scale, int scale_dtype, void* out, int out_dtype, int N, int K,
                  gfx_stream_t stream);
+
+/* int4_dequant with a choice of scale block: qblock 32 (scales [N, K/32]) or
+ * 16 (scales [N, K/16], the reference's qblock=16 format,
+ * int4_gemm_scaled.hip:153-160); same arithmetic. */
+int int4_dequant_qblock(const void* w_q4, const void* w_scale, int scale_dtype, int qblock, void* out, int out_dtype,
+                        int N, int K, gfx_stream_t stream);
 
 /* Convert float32 scales to float16 and count the ones that did not survive
  * the round trip exactly (*inexact, a device int, is overwritten). */

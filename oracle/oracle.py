@@ -10,10 +10,13 @@ reference's own Python (``nodes/ComfyUI-Gfx906Int4/ops.py`` with a one-class
 ``comfy.ops`` stub, ``nodes.py`` with module stubs, and the harness helpers
 ``develop/experiments/2026-10-11/int4_train_test.py:46-52`` /
 ``develop/harness/bench_int8.py:32-33`` extracted verbatim). The reference's
-HIP quantizers (``int4_gemm_scaled.hip:197-220``, ``int8_gemm.hip:217-246``)
-cannot run here (gfx906 only); their restatements are pinned only through the
-torch-semantics twin they document (``quantize_pack_int4`` with a reciprocal
-divide), which is called out per function.
+HIP quantizers and block-scaled integer GEMMs (``int4_gemm_scaled.hip``,
+``int8_gemm.hip``) are gfx906 code; ``oracle/build_ref.py`` compiles those
+sources unmodified for the B200 against a HIP stand-in header
+(``oracle/hip_shim``), and ``tests/test_reference_kernels_gpu.py`` pins
+``quantize_pack_int4`` (div_mode "recip"), ``quantize_int8`` and
+``block_int_matmul`` bit for bit against the reference's own kernels run
+there.
 
 Layouts (reference ``ops.py:108-126``, ``csrc/int4_gemm_scaled.hip:6-10``):
   * native int4: int8 ``[N, K/2]``, two's-complement nibbles, interleaved:
@@ -229,34 +232,52 @@ def dequant_int8(q: np.ndarray, s: np.ndarray, block: int = BLOCK) -> np.ndarray
 # ---------------------------------------------------------------------------
 # GEMM oracles (fp32 dequant then fp32 matmul: bench_int8.py:43)
 # ---------------------------------------------------------------------------
-def w4a16_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None) -> np.ndarray:
-    """``Y = X.float() @ dequant(W).T (+ bias)`` in fp32."""
-    w = dequant_int4(packed, scale)
+def w4a16_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None, block: int = BLOCK) -> np.ndarray:
+    """``Y = X.float() @ dequant(W).T (+ bias)`` in fp32 (``block`` = the scale
+    block, 32 or the reference's qblock=16)."""
+    w = dequant_int4(packed, scale, block)
     y = np.asarray(x, dtype=np.float32) @ w.T
     if bias is not None:
         y = y + np.asarray(bias, dtype=np.float32)
     return y
 
 
-def w4a16_matmul_bf16w(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None) -> np.ndarray:
+def w4a16_matmul_bf16w(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None,
+                       block: int = BLOCK) -> np.ndarray:
     """``Y = X.float() @ bf16(dequant(W)).T`` in fp32: the W4A16 emulation with
     the weight rounded to bf16 (nodes.py:51-52 for a bf16 model). The
     tensor-core kernel multiplies exactly these operands, so it matches this
     oracle up to fp32 accumulation order."""
-    w = round_to_bf16(dequant_int4(packed, scale))
+    w = round_to_bf16(dequant_int4(packed, scale, block))
     y = np.asarray(x, dtype=np.float32) @ w.T
     if bias is not None:
         y = y + np.asarray(bias, dtype=np.float32)
     return y
 
 
+def _fmaf(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
+    """C's fmaf on float32 arrays: a * b + c with one rounding to float32. The
+    product of an integer dot (<= 43 bits with the fp32 factor) is exact in
+    x86 extended precision (64-bit mantissa); the sum is rounded there and
+    then to float32, which equals a single rounding except when the extended
+    sum lands exactly on a float32 tie after being rounded itself."""
+    ld = np.longdouble
+    return (np.asarray(a).astype(ld) * np.asarray(b).astype(ld) + np.asarray(c).astype(ld)).astype(np.float32)
+
+
 def block_int_matmul(ca: np.ndarray, sa: np.ndarray, cb: np.ndarray, sb: np.ndarray, bias=None,
-                     block: int = BLOCK) -> np.ndarray:
+                     block: int = BLOCK, splits: int = 1) -> np.ndarray:
     """The reference's block-scaled integer GEMM (gemm_int4 and gemm_int8:
-    int4_gemm_scaled.hip:147-152, int8_gemm.hip:190-194): integer codes
-    ca [M, K], cb [N, K], fp32 block scales sa [M, K/block], sb [N, K/block];
+    int4_gemm_scaled.hip:53-191, int8_gemm.hip:176-194): integer codes
+    ca [M, K], cb [N, K], fp32 block scales sa [M, K/block], sb [N, K/block]
+    (block 32, or 16 for gemm_int4's qblock=16, where each 32-element load
+    splits into two rescaled 16-element dots, int4_gemm_scaled.hip:153-160);
     per block the exact integer dot product, ``acc = fmaf(dot, sa * sb, acc)``
-    in block order (one split), then + bias."""
+    in block order from acc = 0, bias added last in fp32. With ``splits`` > 1
+    (gemm_int4's split-K, int4_gemm_scaled.hip:228-246) the K stages of 128
+    elements are cut into ceil(stages / splits)-stage slices, each slice's
+    partial is such a chain, and the partials are summed in slice order from
+    0.0 before the bias (splitk_reduce_kernel, :182-191)."""
     ca = np.asarray(ca).astype(np.int64)
     cb = np.asarray(cb).astype(np.int64)
     M, K = ca.shape
@@ -265,13 +286,24 @@ def block_int_matmul(ca: np.ndarray, sa: np.ndarray, cb: np.ndarray, sb: np.ndar
     dots = np.einsum("mbk,nbk->mnb", ca.reshape(M, nb, block), cb.reshape(N, nb, block))  # exact integers
     sab = (np.asarray(sa, np.float32).reshape(M, nb)[:, None, :] *
            np.asarray(sb, np.float32).reshape(N, nb)[None, :, :]).astype(np.float32)
-    acc = np.zeros((M, N), dtype=np.float32)
-    for b in range(nb):  # fmaf: exact product + sum in float64, one rounding to float32
-        acc = (dots[:, :, b].astype(np.float64) * sab[:, :, b].astype(np.float64) + acc.astype(np.float64)).astype(
-            np.float32)
+    k_stages = -(-K // 128)
+    per = -(-k_stages // splits)
+    bounds = [(s * per * 128 // block, min(nb, (s + 1) * per * 128 // block)) for s in range(splits)]
+    parts = []
+    for b0, b1 in bounds:
+        acc = np.zeros((M, N), dtype=np.float32)
+        for b in range(b0, b1):
+            acc = _fmaf(dots[:, :, b].astype(np.float32), sab[:, :, b], acc)
+        parts.append(acc)
+    if splits == 1:
+        out = parts[0]
+    else:
+        out = np.zeros((M, N), dtype=np.float32)
+        for p_ in parts:
+            out = (out + p_).astype(np.float32)
     if bias is not None:
-        acc = acc + np.asarray(bias, dtype=np.float32)
-    return acc
+        out = (out + np.asarray(bias, dtype=np.float32)).astype(np.float32)
+    return out
 
 
 def w4a4_matmul(x: np.ndarray, packed: np.ndarray, scale: np.ndarray, bias=None, block: int = BLOCK) -> np.ndarray:

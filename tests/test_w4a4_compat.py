@@ -88,11 +88,32 @@ def test_gemm_int4_reference_op(cuda, M):
                              bias.cpu().numpy())
     m = O.parity_metrics(y.cpu().numpy(), ref)
     assert m["max_abs_over_max_ref"] <= 2e-2 and m["mean_rel"] <= 5e-3, m
-    with pytest.raises(RuntimeError, match="qblock=16"):
-        ops.gemm_int4(A, As.reshape(-1).repeat_interleave(2), torch.from_numpy(p).to(cuda),
-                      torch.from_numpy(s).reshape(-1).repeat_interleave(2).to(cuda), None, torch.float32, qblock=16)
     with pytest.raises(RuntimeError, match="scales must be"):
         ops.gemm_int4(A, As[:, :1], torch.from_numpy(p).to(cuda), torch.from_numpy(s).to(cuda), None, torch.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [2, 64, 200])
+def test_gemm_int4_qblock16_reference_op(cuda, M):
+    """ops.gemm_int4(..., qblock=16): A and B with one scale per 16 elements
+    (int4_gemm_scaled.hip:153-160, SUB = 2: each 32-element load splits into
+    two 16-element dot products, each rescaled), against the integer-block
+    formula over 16-element blocks."""
+    from comfy_ui_gfx906_tools_b200 import ops
+    N, K = 320, 768
+    rng = np.random.default_rng(40 + M)
+    ca, cb = rng.integers(-8, 8, (M, K)), rng.integers(-8, 8, (N, K))
+    sa = ((np.abs(rng.normal(0, 1, (M, K // 16))) + 0.05) * 0.2).astype(np.float32)
+    sb = (np.abs(rng.normal(0, 0.01, (N, K // 16))) + 1e-4).astype(np.float32)
+    bias = torch.linspace(-1, 1, N, device=cuda)
+    A, B = torch.from_numpy(O.pack_int4_codes(ca)).to(cuda), torch.from_numpy(O.pack_int4_codes(cb)).to(cuda)
+    y = ops.gemm_int4(A, torch.from_numpy(sa).to(cuda), B, torch.from_numpy(sb).to(cuda), bias, torch.float32,
+                      qblock=16)
+    ref = O.block_int_matmul(ca, sa, cb, sb, bias.cpu().numpy(), block=16)
+    m = O.parity_metrics(y.cpu().numpy(), ref)
+    assert m["max_abs_over_max_ref"] <= 2e-2 and m["mean_rel"] <= 5e-3, m
+    with pytest.raises(RuntimeError, match="scales must be"):
+        ops.gemm_int4(A, torch.from_numpy(sa).to(cuda), B, torch.from_numpy(sb).to(cuda), None, torch.float32)
 
 
 @pytest.mark.gpu
