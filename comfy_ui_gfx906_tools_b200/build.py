@@ -61,9 +61,12 @@ def needs_build() -> bool:
     return _newest(_sources() + _headers() + [os.path.abspath(__file__)]) > os.path.getmtime(LIB_PATH)
 
 
-def _compile(src: str, verbose: bool, extra=(), obj_dir: str = OBJ_DIR) -> str:
+def _compile(src: str, verbose: bool, extra=(), obj_dir: str = OBJ_DIR, force: bool = True) -> str:
     os.makedirs(obj_dir, exist_ok=True)
     obj = os.path.join(obj_dir, os.path.basename(src).replace(".cu", ".o"))
+    if not force and os.path.exists(obj) and os.path.getmtime(obj) >= _newest(
+            [src, *_headers(), os.path.abspath(__file__)]):
+        return obj  # up to date (default flags only)
     cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
     if verbose:
         cmd += ["-Xptxas", "-v"]
@@ -84,8 +87,9 @@ def build(force: bool = False, verbose: bool = False, defines=(), out_path: str 
     os.makedirs(os.path.dirname(target), exist_ok=True)
     srcs = _sources()
     obj_dir = OBJ_DIR if not defines else os.path.join(OBJ_DIR, "variant_" + str(abs(hash(tuple(defines)))))
+    incremental = not force and not defines and not verbose
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose, tuple(defines), obj_dir), srcs))
+        objs = list(ex.map(lambda s: _compile(s, verbose, tuple(defines), obj_dir, force=not incremental), srcs))
     tmp = target + ".tmp"
     cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lrt", "-lpthread", "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -39,6 +39,7 @@ int launch_w4a16_smallm_targets(const void* x, const void* wq, const void* ws, i
                                 const OutTargets& out, int out_dtype, int M, int N, int K, int splits,
                                 void* workspace, size_t workspace_bytes, cudaStream_t stream, int sms);
 int launch_peer_barrier(int* const* flags, int n_ranks, int rank, cudaStream_t stream);
+
 size_t smallm_workspace_bytes(int M, int N, int K, int splits, int sms);
 int smallm_auto_splits(int M, int N, int K, int sms);
 int smallm_device_status(int clear);

@@ -324,14 +324,16 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
       if constexpr (kCl) cluster_sync_all();
       return;
     }
-    const uint8_t* st = smem + stage * L::kStageBytes;
-    const uint32_t nib_base = smem_u32(st);
-    const uint8_t* sc = st + L::kNibBytes;
+    // explicit shared-window addresses (generic pointers into shared memory
+    // can compile to generic loads, with L1TEX latency)
+    const uint32_t st_s = smem_u32(smem) + stage * L::kStageBytes;
+    const uint32_t nib_base = st_s;
+    const uint32_t sc_s = st_s + L::kNibBytes;
 #pragma unroll
     for (int gi = 0; gi < kGPW; ++gi) {
       const int grp = kq * kGPW + gi;
       const int h = grp & 1;  // which 32-group of x box grp/2
-      const uint8_t* xs = sc + L::kScaleBytes + (grp >> 1) * L::kXBoxBytes;
+      const uint32_t xs_s = sc_s + L::kScaleBytes + (grp >> 1) * L::kXBoxBytes;
       // All shared-memory loads of this group first (volatile ldmatrix keeps
       // source order, so loads written after an MMA could not start earlier):
       // the activation fragments, one nibble word per row and m16 tile, and
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
       for (int nt = 0; nt < NT; ++nt) {
         const int row = nt * 8 + xrow_in_tile;
         const int chunk = h * 4 + t_;
-        xv[nt] = *reinterpret_cast<const uint4*>(xs + row * 128 + ((chunk ^ (row & 7)) << 4));
+        xv[nt] = lds128(xs_s + row * 128 + ((chunk ^ (row & 7)) << 4));
       }
       uint32_t wr[kMT], wr8[kMT];
 #pragma unroll
@@ -355,13 +357,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
       for (int mt = 0; mt < kMT; ++mt) {
         const int r_lo = rs * 16 * kMT + mt * 16 + g_, r_hi = r_lo + 8;
         if (kF16Scale) {
-          const __half* sch = reinterpret_cast<const __half*>(sc);
-          s_r[mt] = __half2float(sch[r_lo * kGroupsPerStage + grp]);
-          s_r8[mt] = __half2float(sch[r_hi * kGroupsPerStage + grp]);
+          s_r[mt] = lds_f16_as_f32(sc_s + (r_lo * kGroupsPerStage + grp) * 2);
+          s_r8[mt] = lds_f16_as_f32(sc_s + (r_hi * kGroupsPerStage + grp) * 2);
         } else {
-          const float* scf = reinterpret_cast<const float*>(sc);
-          s_r[mt] = scf[r_lo * kGroupsPerStage + grp];
-          s_r8[mt] = scf[r_hi * kGroupsPerStage + grp];
+          s_r[mt] = lds_f32(sc_s + (r_lo * kGroupsPerStage + grp) * 4);
+          s_r8[mt] = lds_f32(sc_s + (r_hi * kGroupsPerStage + grp) * 4);
         }
       }
       // B fragments and the offset correction p0 = -136 * sum_k x (constant A operand).
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     // every consumer is done reading it, it doubles as the reduction buffer.
     // Layout [quarter-1][element][slice*32 + lane]: consecutive lanes write
     // consecutive words (no bank conflicts).
-    float* red = reinterpret_cast<float*>(const_cast<uint8_t*>(st));
+    const uint32_t red_s = st_s;  // float index i at red_s + 4 i
     constexpr int kRedStride = kRowSlices * 32;                     // floats per element row
     constexpr int kRedQuarter = L::kAcc * kRedStride;               // floats per K quarter
     constexpr bool kOneRound = (kKParts - 1) * kRedQuarter * 4 <= L::kStageBytes;
@@ -424,25 +424,26 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
     // 1) K parts 1.. -> part 0
     if (kOneRound) {
       if (kq != 0) {
-        float* dst = red + (kq - 1) * kRedQuarter + rl;
+        const uint32_t dst = red_s + 4u * (uint32_t)((kq - 1) * kRedQuarter + rl);
 #pragma unroll
         for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dst[((mt * NT + nt) * 4 + e) * kRedStride] = acc[mt][nt][e];
+            for (int e = 0; e < 4; ++e) sts_f32(dst + 4u * (uint32_t)(((mt * NT + nt) * 4 + e) * kRedStride), acc[mt][nt][e]);
       }
       consumer_sync();
       if (kq == 0) {
 #pragma unroll
         for (int q = 0; q < kKParts - 1; ++q) {
-          const float* src = red + q * kRedQuarter + rl;
+          const uint32_t src = red_s + 4u * (uint32_t)(q * kRedQuarter + rl);
 #pragma unroll
           for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int e = 0; e < 4; ++e) acc[mt][nt][e] += src[((mt * NT + nt) * 4 + e) * kRedStride];
+              for (int e = 0; e < 4; ++e)
+                acc[mt][nt][e] += lds_f32(src + 4u * (uint32_t)(((mt * NT + nt) * 4 + e) * kRedStride));
         }
       }
     } else {
@@ -454,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int e = 0; e < 4; ++e) red[((mt * NT + nt) * 4 + e) * kRedStride + rl] = acc[mt][nt][e];
+              for (int e = 0; e < 4; ++e)
+                sts_f32(red_s + 4u * (uint32_t)(((mt * NT + nt) * 4 + e) * kRedStride + rl), acc[mt][nt][e]);
         }
         consumer_sync();
         if (kq == 0) {
@@ -463,7 +465,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? GFX_SMALLM_CTAS_PER_SM : (
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int e = 0; e < 4; ++e) acc[mt][nt][e] += red[((mt * NT + nt) * 4 + e) * kRedStride + rl];
+              for (int e = 0; e < 4; ++e)
+                acc[mt][nt][e] += lds_f32(red_s + 4u * (uint32_t)(((mt * NT + nt) * 4 + e) * kRedStride + rl));
         }
         consumer_sync();
       }
@@ -686,6 +689,7 @@ size_t smallm_workspace_bytes(int M, int N, int K, int splits_req, int sms) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   // sized for the larger of the fp16 / fp32 scale plans
   size_t need = 0;
+
   for (int f = 0; f < 2; ++f) {
     SmallMPlan p = smallm_plan(M, N, K, splits_req, sms, f == 1);
     const size_t part = (size_t)p.tok_blocks * p.RB * p.max_segs * p.tok * smallm::kRows * sizeof(float);

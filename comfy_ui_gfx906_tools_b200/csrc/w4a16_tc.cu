@@ -273,26 +273,11 @@ __device__ __forceinline__ uint2 dequant_int8_word(uint32_t w, float s) {
   return make_uint2(pack_bf16x2_rn(f[0], f[1]), pack_bf16x2_rn(f[2], f[3]));
 }
 
-// Explicit shared-window accesses: the stage pointers are generic, and generic
-// 16-byte accesses to shared memory measured ~58% extra store wavefronts (bank
-// conflicts) on the dequantized-weight stores; st.shared / ld.shared with a
-// 32-bit shared address issue STS.128 / LDS.128.
-__device__ __forceinline__ void sts128(uint32_t addr, const uint4& v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
-
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
-               : "memory");
-  return v;
-}
-
 struct Smem {
   uint8_t* stage0;     // stage s starts at stage0 + s * kStageBytes
   uint8_t* chunk0;     // scale chunk b starts at chunk0 + b * kChunkBytes
-  uint64_t* full;      // [kStages] TMA (+ cp.async scales) landed
+  uint64_t* full;      // [kStages] packed weights (+ cp.async scales) landed; with a pair, the x slice too
+  uint64_t* xfull;     // [kStages] one CTA: the x tile landed (the dequant does not wait for it)
   uint64_t* wready;    // [kStages] dequantized weights written
   uint64_t* empty;     // [kStages] MMAs done reading the stage
   uint64_t* acc_full;  // [2]
@@ -330,13 +315,14 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   sm.full = bars;
   sm.wready = bars + kStages;
   sm.empty = bars + 2 * kStages;
-  sm.acc_full = bars + 3 * kStages;
-  sm.acc_empty = bars + 3 * kStages + 2;
-  sm.drain = bars + 3 * kStages + 4;
-  sm.sfull = bars + 3 * kStages + 5;
-  sm.sempty = bars + 3 * kStages + 7;
-  sm.tmem_base = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 9);
-  static_assert((3 * kStages + 9) * 8 + 4 <= kBarrierBytes, "barrier area");
+  sm.xfull = bars + 3 * kStages;
+  sm.acc_full = bars + 4 * kStages;
+  sm.acc_empty = bars + 4 * kStages + 2;
+  sm.drain = bars + 4 * kStages + 4;
+  sm.sfull = bars + 4 * kStages + 5;
+  sm.sempty = bars + 4 * kStages + 7;
+  sm.tmem_base = reinterpret_cast<uint32_t*>(bars + 4 * kStages + 9);
+  static_assert((4 * kStages + 9) * 8 + 4 <= kBarrierBytes, "barrier area");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -353,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], (T::kChannel || stma) ? 1 : 1 + 32);
+      mbar_init(&sm.xfull[s], 1);
       mbar_init(&sm.wready[s], kDequantWarps / kG * C);  // one group; a pair's arrive on CTA 0
       mbar_init(&sm.empty[s], 1);
     }
@@ -412,9 +399,15 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
         }
         uint8_t* st = sm.stage0 + s * kStageBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full[s], kXBytes + T::kQBytes);
-          tma_load_2d(st, &x_map, &sm.full[s], ks * kStageK, m0);
+          // One CTA: the packed weights on full[s] (all the dequant waits for,
+          // issued first) and the x tile on xfull[s] (only the MMA waits for
+          // it). A pair keeps both on full[s]: CTA 1's dequant warps vouch for
+          // its x slice when they arrive on CTA 0's wready.
+          uint64_t* xbar = C == 1 ? &sm.xfull[s] : &sm.full[s];
+          mbar_arrive_expect_tx(&sm.full[s], T::kQBytes + (C == 1 ? 0 : kXBytes));
           tma_load_2d(st + kXBytes + kWBytes, &q_map, &sm.full[s], ks * T::kQRowBytes, n0);
+          if (C == 1) mbar_arrive_expect_tx(xbar, kXBytes);
+          tma_load_2d(st, &x_map, xbar, ks * kStageK, m0);
         }
         if (!T::kChannel && !stma) {
           // cp.async fallback: this stage's scales into its [row][group] area,
@@ -456,6 +449,13 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     const int dt = (warp - kDequantWarp0) * 32 + lane;
     const int q = dt / kGroupThreads, wg = (dt % kGroupThreads) >> 5;
     const int r_in = (lane & 7) + 8 * (lane >> 4), g = (lane >> 3) & 1;
+    // fp16 scales by TMA: each thread keeps its rows' 16-byte chunk rows (8
+    // scales) in registers across its group's stages of the chunk, loaded
+    // once with a conflict-free 16-byte load (a 2-byte load per stage from
+    // 16-byte rows is a 2-way bank conflict between rows r and r + 8)
+    uint4 scache[kRounds];
+#pragma unroll
+    for (int rd = 0; rd < kRounds; ++rd) scache[rd] = make_uint4(0u, 0u, 0u, 0u);
     uint32_t kit = 0;
     for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
       for (int ks = 0; ks < k_stages; ++ks, ++kit) {
@@ -476,6 +476,15 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
           sbase = sm.chunk0 + (c & 1) * T::kChunkBytes;
           srow_bytes = T::kChunkRowBytes;
           sgroup0 = (int)(kit % kCS) * T::kGroupsPerStage;
+          if constexpr (T::kF16Group) {
+            if ((int)(kit % kCS) < kG) {  // this group's first stage of the chunk
+#pragma unroll
+              for (int rd = 0; rd < kRounds; ++rd) {
+                const int blk = rd * kWarpsPerGroup + wg;
+                if (blk < kTileN / 16) scache[rd] = lds128(smem_u32(sbase) + (blk * 16 + r_in) * T::kChunkRowBytes);
+              }
+            }
+          }
         } else {
           sbase = qt + T::kQBytes;
           srow_bytes = T::kGroupsPerStage * T::kScaleElem;
@@ -499,7 +508,14 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
               sf = reinterpret_cast<const float*>(srow)[sgroup0 + 2 * g];
               sf1 = reinterpret_cast<const float*>(srow)[sgroup0 + 2 * g + 1];
             } else if constexpr (T::kF16Group) {
-              sf = __half2float(reinterpret_cast<const __half*>(srow)[sgroup0 + g]);
+              if (stma) {
+                const uint4 cv = scache[rd];
+                const int k4 = (int)(kit % kCS);
+                const uint32_t w = k4 == 0 ? cv.x : (k4 == 1 ? cv.y : (k4 == 2 ? cv.z : cv.w));
+                sf = __half2float(__ushort_as_half((unsigned short)(g ? (w >> 16) : (w & 0xFFFFu))));
+              } else {
+                sf = __half2float(reinterpret_cast<const __half*>(srow)[sgroup0 + g]);
+              }
               const float hi = __uint_as_float(__float_as_uint(sf) & 0xFFFF0000u);
               const float lo = sf - hi;  // exact; at most 3 significant bits for an fp16 value
               const uint32_t hb = __float_as_uint(hi) >> 16;
@@ -561,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
           const int s = kit % kStages;
           const uint32_t ph = (kit / kStages) & 1;
           // wready[s] complete => every arriving dequant warp saw its CTA's full[s]
-          if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout) ||
+          if (!mbar_wait(C == 1 ? &sm.xfull[s] : &sm.full[s], ph, kDevErrFullBarrierTimeout) ||
               !mbar_wait(&sm.wready[s], ph, kDevErrFullBarrierTimeout)) {
             ok = false;
             break;
