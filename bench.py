@@ -265,7 +265,10 @@ def make_weights(dev, seed):
     return ws
 
 
-def time_steps(fn, steps, warmup, world, dev, stream, soak_s=0.0):
+def time_steps(fn, steps, warmup, world, dev, stream, soak_s=0.0, on_step=None):
+    """Device time of `steps` back-to-back calls of fn (CUDA events on the
+    launching stream, barrier + synchronize on both sides). on_step(k), when
+    given, is called before timed step k (k = -1 for warm-up and soak)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(dev)
@@ -279,12 +282,16 @@ def time_steps(fn, steps, warmup, world, dev, stream, soak_s=0.0):
     torch.cuda.synchronize(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(steps):
+    for k in range(steps):
+        if on_step is not None:
+            on_step(k)
         fn()
     b.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
+    if on_step is not None:
+        on_step(-1)
     return a.elapsed_time(b)
 
 
@@ -322,18 +329,23 @@ def run_ours(args, world, rank, local):
     yfull = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for (_, _, N, _, _) in weights] if world > 1 else None
 
     # --- device-resident timed loop ---
-    launch_ms = [0.0] * len(weights)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in weights]
-    record = {"on": False}
+    # per-launch CUDA events inside the timed region itself (same clocks and
+    # back-to-back regime as the step time; one event pair per launch)
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in weights] for _ in range(args.steps)]
+    record = {"k": -1}
+
+    def on_step(k):
+        record["k"] = k
 
     def step():
         works = []
+        k = record["k"]
         for i, ((_, K, N, p, s), x) in enumerate(zip(weights, xloc)):
-            if record["on"]:
-                ev[i][0].record(stream)
+            if k >= 0:
+                ev[k][i][0].record(stream)
             y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
-            if record["on"]:
-                ev[i][1].record(stream)
+            if k >= 0:
+                ev[k][i][1].record(stream)
             if world > 1:  # this GEMM's rows to every rank, overlapped with the next GEMM
                 works.append(dist.all_gather_into_tensor(yfull[i], y, async_op=True))
         for w in works:
@@ -341,18 +353,11 @@ def run_ours(args, world, rank, local):
 
     clocks = ClockSampler(dev.index)
     with clocks:
-        ms_total = time_steps(step, args.steps, args.warmup, world, dev, stream, soak_s=1.0)
+        ms_total = time_steps(step, args.steps, args.warmup, world, dev, stream, soak_s=1.0, on_step=on_step)
     ms_total = max_over_ranks(ms_total, world, dev)
     ms_step = ms_total / args.steps
     value = flops_step / (ms_step * 1e-3) / 1e12
-    # per-launch kernel durations on the launching stream, in a second pass
-    record["on"] = True
-    for _ in range(args.steps):
-        step()
-        torch.cuda.synchronize(dev)
-        for i in range(len(weights)):
-            launch_ms[i] += ev[i][0].elapsed_time(ev[i][1])
-    record["on"] = False
+    launch_ms = [sum(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(args.steps)) for i in range(len(weights))]
     avg_launch_ms = sum(launch_ms) / (args.steps * len(weights))
     achieved = (flops_step / world / len(weights)) / (avg_launch_ms * 1e-3) / 1e12
     traffic = None
