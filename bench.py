@@ -436,6 +436,24 @@ def run_ours(args, world, rank, local):
                 "frac_of_burst_peak": (flops_step / (ms8 * 1e-3) / 1e12) / pk["bf16_tflops"]}
         del w8
 
+    # --- the reference's own W4A4 numerics (gemm_int4, integer-exact, bit-identical to the
+    # reference's kernel; tests/test_w4a4_exact_gpu.py): the six shapes at M=4608 on int4
+    # activations from quantize_int4 and the same packed weights with fp32 scales ---
+    w4a4 = None
+    if not args.no_int8 and world == 1:
+        xq = [ops.quantize_int4(x) for x in xs]
+        w32 = [(p, s.float()) for (_, _, _, p, s) in weights]
+
+        def step4():
+            for (a, sa), (p, s) in zip(xq, w32):
+                ops.gemm_int4(a, sa, p, s, None, torch.bfloat16)
+        ms4 = time_steps(step4, args.steps, args.warmup, world, dev, stream) / args.steps
+        w4a4 = {"value": flops_step / (ms4 * 1e-3) / 1e12, "unit": "TOPS (int4 x int4, 2*M*N*K)", "ms_per_step": ms4,
+                "numerics": "bit-identical to the reference's int4_gemm_kernel (integer block dots on tcgen05 "
+                            "kind::f8f6f4, the reference's fp32 chain and split plan)",
+                "includes": "per call: e5m2 pre-pass of A, scale transpose, the GEMM"}
+        del xq, w32
+
     # --- e2e: public API with host buffers, H2D of x and D2H of y inside the timed region ---
     # (pinned host buffers; the copies of one step overlap its GEMMs and each other)
     e2e = None
@@ -503,7 +521,7 @@ def run_ours(args, world, rank, local):
             "parity": {"ok": parity_ok, "rows_sampled": 64, "per_shape": parity,
                        "reference": "torch fp32 dequant-then-matmul of the sampled rows (north-star tolerance "
                                     "2e-2 max-abs ratio, 5e-3 mean relative error)"},
-            "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8,
+            "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8, "w4a4_exact": w4a4,
             **({"small_m_channel_split": tp} if tp is not None else {}),
             **({"dit_rows": dit} if dit is not None else {}),
             "gpu_launches": args.steps * len(weights), "clocks": clocks.summary(),
@@ -658,11 +676,16 @@ def run_case(args):
         ws.append((p, s))
     x = synthetic.activations(args.m, K, seed=1).to(dev)
     stream = torch.cuda.Stream(dev)
+    if args.w4a4:  # the integer-exact W4A4 GEMM: int4 activations from quantize_int4, fp32 weight scales
+        xa, xs = ops.quantize_int4(x)
+        ws = [(p, s.float()) for p, s in ws]
 
     def run():
         for i in range(args.reps):
             p, s = ws[i % args.copies]
-            if args.int8:
+            if args.w4a4:
+                ops.gemm_int4(xa, xs, p, s, None, torch.bfloat16, splits=args.splits)
+            elif args.int8:
                 ops.gemm_w8a16(x, p8[i % args.copies][0], p8[i % args.copies][1], None, torch.bfloat16)
             else:
                 ops.gemm_w4a16(x, p, s, None, torch.bfloat16, splits=args.splits)
@@ -687,6 +710,14 @@ def run_case(args):
         torch.cuda.synchronize(dev)
     us = 1e3 * e0.elapsed_time(e1) / args.reps
     sb = 2 if args.int8 else ws[0][1].element_size()
+    if args.w4a4:  # packed A + its fp32 scales instead of bf16 x
+        nbytes = N * K // 2 + N * (K // 32) * 4 + args.m * K // 2 + args.m * (K // 32) * 4 + 2 * args.m * N
+        print(json.dumps({"case": args.case if not (args.n and args.k) else f"{N}x{K}", "M": args.m, "N": N, "K": K,
+                          "us": 1e3 * e0.elapsed_time(e1) / args.reps, "w4a4_exact": True,
+                          "tops": 2 * args.m * N * K / (1e3 * e0.elapsed_time(e1) / args.reps) / 1e6,
+                          "GB_s": nbytes / (1e3 * e0.elapsed_time(e1) / args.reps) / 1e3, "graph": args.graph,
+                          "copies": args.copies, "splits": args.splits}))
+        return
     wbytes = N * K if args.int8 else N * K // 2 + N * (K // 32) * sb
     nbytes = wbytes + 2 * args.m * K + 2 * args.m * N
     print(json.dumps({"case": args.case if not (args.n and args.k) else f"{N}x{K}", "M": args.m, "N": N, "K": K,
@@ -719,6 +750,8 @@ def main():
     ap.add_argument("--fp32-scales", action="store_true")
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--graph", action="store_true", help="case: time a CUDA graph of the reps")
+    ap.add_argument("--w4a4", action="store_true",
+                    help="case: the integer-exact W4A4 GEMM (gemm_int4) on quantize_int4 activations")
     ap.add_argument("--int8", action="store_true", help="case: the int8 (W8A16) kernel, per-channel scales")
     args = ap.parse_args()
     if args.case is not None:

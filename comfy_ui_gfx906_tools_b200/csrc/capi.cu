@@ -240,7 +240,8 @@ int gfx_device_status(int clear) {
   int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return -set_error(GFX_ERR_CUDA, "gfx_device_status: %s", cudaGetErrorString(e));
-  const int parts[3] = {smallm_device_status(clear), tc_device_status(clear), selftest_device_status(clear)};
+  const int parts[4] = {smallm_device_status(clear), tc_device_status(clear), selftest_device_status(clear),
+                         w4a4x_device_status(clear)};
   for (int p : parts) {
     if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
     if (p && !v) v = p;
@@ -307,6 +308,45 @@ int w4a16_gemm_qblock(const void* x, int x_dtype, const void* w_q4, const void* 
   // 16-element groups run on the tensor-core kernel for every M (the
   // reference's qblock=16 GEMMs are its training GEMMs, large M)
   return launch_w4a16_tc(x, w_q4, w_scale, GFX_SCALE_F32, bias, y, out_dtype, M, N, K, st, sm_count(dev), 16);
+}
+
+size_t w4a4_gemm_exact_workspace_bytes(int M, int N, int K, int qblock) {
+  return w4a4_exact_workspace(M, N, K, qblock);
+}
+
+int w4a4_gemm_exact_splits(int M, int N, int K, int splits) {
+  const int dev = current_device();
+  return w4a4_exact_splits(M, N, K, splits, sm_count(dev < 0 ? 0 : dev));
+}
+
+int w4a4_gemm_exact(const void* a_q4, const float* a_scale, const void* b_q4, const float* b_scale, int qblock,
+                    const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+                    size_t workspace_bytes, gfx_stream_t stream) {
+  const char* fn = "w4a4_gemm_exact";
+  if (!a_q4 || !a_scale || !b_q4 || !b_scale || !y)
+    return set_error(GFX_ERR_INVALID, "%s: A, A_scale, B, B_scale and C must be device pointers", fn);
+  if (M < 0 || N <= 0 || K <= 0 || K % 32 != 0)
+    return set_error(GFX_ERR_INVALID, "%s: expected A [M, K/2], B [N, K/2], K %% 32 == 0; got M=%d N=%d K=%d", fn, M,
+                     N, K);
+  if (qblock != 32 && qblock != 16)
+    return set_error(GFX_ERR_INVALID, "%s: qblock must be 32 or 16, got %d", fn, qblock);
+  if (splits < 0 || splits > 8) return set_error(GFX_ERR_INVALID, "%s: splits must be in [0, 8], got %d", fn, splits);
+  if (out_dtype != GFX_DTYPE_F32 && out_dtype != GFX_DTYPE_F16 && out_dtype != GFX_DTYPE_BF16)
+    return set_error(GFX_ERR_INVALID, "%s: unsupported out dtype %d, expected float32/float16/bfloat16", fn, out_dtype);
+  if ((reinterpret_cast<uintptr_t>(a_q4) & 15) || (reinterpret_cast<uintptr_t>(b_q4) & 15) ||
+      (reinterpret_cast<uintptr_t>(b_scale) & 15))
+    return set_error(GFX_ERR_INVALID, "%s: packed A, packed B and B_scale must be 16-byte aligned", fn);
+  if (M == 0) return GFX_OK;
+  const size_t need = w4a4_exact_workspace(M, N, K, qblock);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return set_error(GFX_ERR_INVALID, "%s: needs a 16-byte aligned workspace of %zu bytes (w4a4_gemm_exact_workspace_"
+                     "bytes), got %zu", fn, need, workspace ? workspace_bytes : (size_t)0);
+  const int dev = current_device();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = check_device_health(fn, dev, nullptr, 0, st);
+  if (rc) return rc;
+  return launch_w4a4_exact(a_q4, a_scale, b_q4, b_scale, qblock, bias, y, out_dtype, M, N, K, splits, workspace, st,
+                           sm_count(dev));
 }
 
 int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,

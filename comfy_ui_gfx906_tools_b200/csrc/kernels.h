@@ -54,6 +54,16 @@ int selftest_device_status(int clear);
 int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 
+// integer-exact W4A4 (the reference's int4 x int4 block GEMM, bit for bit) -- w4a4_exact.cu
+// a_q4 [M, K/2] / b_q4 [N, K/2] packed int4, fp32 scales [M|N, K/qblock]; workspace of
+// w4a4_exact_workspace(M, N, K, qblock) bytes, 16-byte aligned. splits 0 = the reference's plan.
+size_t w4a4_exact_workspace(int M, int N, int K, int qblock);
+int w4a4_exact_splits(int M, int N, int K, int splits, int sms);
+int launch_w4a4_exact(const void* a_q4, const float* a_scale, const void* b_q4, const float* b_scale, int qblock,
+                      const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+                      cudaStream_t stream, int sms);
+int w4a4x_device_status(int clear);
+
 // loaders / helpers -- pack.cu
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
                         cudaStream_t stream, int qblock = 32);

@@ -312,8 +312,15 @@ def scales_to_f16_if_exact(w_scale: torch.Tensor):
 # GEMM entry points
 # ---------------------------------------------------------------------------
 def gemm_int4_auto_splits(M: int, N: int, K: int) -> int:
-    """Split-K count the W4A16 GEMM picks for [M, K] x [N, K]^T on the current
-    device (the counterpart of gemm_int4_auto_splits, binding.cpp:358-361)."""
+    """Split-K count ``gemm_int4(..., splits=0)`` uses for [M, K] x [N, K]^T on
+    the current device: the reference's auto_splits (binding.cpp:36-43,
+    exported as gemm_int4_auto_splits, binding.cpp:358-361), evaluated with
+    this device's SM count. The count is part of gemm_int4's numerics."""
+    return int(_lib.load().w4a4_gemm_exact_splits(int(M), int(N), int(K), 0))
+
+
+def gemm_w4a16_auto_splits(M: int, N: int, K: int) -> int:
+    """Split-K count the W4A16 GEMM (``gemm_w4a16``) picks on the current device."""
     return int(_lib.load().w4a16_auto_splits(int(M), int(N), int(K)))
 
 
@@ -466,16 +473,33 @@ def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, 
     return out.reshape(*shape[:-1], w_packed.shape[0])
 
 
+_exact_ws_lock = threading.Lock()
+_exact_workspaces: dict = {}
+
+
+def _exact_workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Scratch of the integer-exact GEMM per (device, stream): the e5m2 copy of
+    A and its transposed scales, rewritten by every call (no state kept)."""
+    key = (device.index, stream)
+    with _exact_ws_lock:
+        ws = _exact_workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _exact_workspaces[key] = ws
+        return ws
+
+
 def gemm_int4(A_packed: torch.Tensor, A_scale: torch.Tensor, B_packed: torch.Tensor, B_scale: torch.Tensor,
               bias: torch.Tensor | None, out_dtype: torch.dtype, splits: int = 0, qblock: int = 32) -> torch.Tensor:
     """The reference's block-scaled int4 GEMM op (``ext.gemm_int4``,
-    binding.cpp:73-112), same arguments, checks and messages: A_packed /
-    A_scale from ``quantize_int4`` (int4 activations), B the packed weight.
-    The A codes are dequantized exactly to bf16 (one rounding of code * scale)
-    and multiplied on the W4A16 kernels; the result matches the reference's
-    integer-block GEMM within bf16 rounding. qblock=16
-    (16-element scale blocks, scales [M, K/16] / [N, K/16]) dequantizes A per
-    16-group and runs the tensor-core kernel's 16-group weight format."""
+    binding.cpp:73-112): same arguments, checks and messages, and the same
+    result bit for bit. A_packed / A_scale come from ``quantize_int4`` (int4
+    activations), B is the packed weight; per output the fp32 chain
+    acc = fmaf(dot, a_scale * b_scale, acc) runs over 32-element blocks (two
+    16-element halves for qblock=16, int4_gemm_scaled.hip:147-160), each of
+    the ``splits`` K slices from zero, slices summed in order, then the bias
+    (splits=0: the reference's auto_splits, see ``gemm_int4_auto_splits``).
+    The block dot products run on the tensor cores (C ABI ``w4a4_gemm_exact``)."""
     if not (A_packed.is_cuda and B_packed.is_cuda):
         raise RuntimeError("inputs must be on device")
     if A_packed.device != B_packed.device:
@@ -494,13 +518,26 @@ def gemm_int4(A_packed: torch.Tensor, A_scale: torch.Tensor, B_packed: torch.Ten
     if A_scale.numel() != M * K // qblock or B_scale.numel() != N * K // qblock:
         raise RuntimeError(f"scales must be [M, K/{qblock}] / [N, K/{qblock}] = {M * K // qblock} / "
                            f"{N * K // qblock} elements, got {A_scale.numel()} / {B_scale.numel()}")
-    if splits < 0 or splits > 16:
-        raise RuntimeError(f"splits must be in [0, 16], got {splits}")
+    dev = A_packed.device
+    C = torch.empty(M, N, dtype=out_dtype, device=dev)
     if M == 0:
-        return torch.empty(0, N, dtype=out_dtype, device=A_packed.device)
-    xa = dequantize_int4(A_packed.contiguous(), A_scale.reshape(M, K // qblock).contiguous(), torch.bfloat16,
-                         block=qblock)
-    return gemm_w4a16(xa, B_packed, B_scale.reshape(N, K // qblock), bias, out_dtype, splits=splits, qblock=qblock)
+        return C
+    if bias is not None:
+        if bias.dtype != out_dtype:
+            raise RuntimeError(f"bias dtype {bias.dtype} != out dtype {out_dtype}")
+        bias = bias.to(dev).contiguous()
+    if splits < 0 or splits > 8:
+        raise RuntimeError(f"splits must be in [0, 8], got {splits}")
+    A, B = A_packed.contiguous(), B_packed.contiguous()
+    As, Bs = A_scale.contiguous(), B_scale.contiguous()
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        nbytes = int(_lib.load().w4a4_gemm_exact_workspace_bytes(M, N, K, qblock))
+        ws = _exact_workspace(dev, st, nbytes)
+        _call_gemm("w4a4_gemm_exact", dev, A.data_ptr(), As.data_ptr(), B.data_ptr(), Bs.data_ptr(), qblock,
+                   bias.data_ptr() if bias is not None else None, C.data_ptr(), _dtype_code(out_dtype), M, N, K,
+                   int(splits), ws.data_ptr(), ws.numel(), st)
+    return C
 
 
 def gemm_int8(A: torch.Tensor, A_scale: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
@@ -535,21 +572,17 @@ def gemm_int8(A: torch.Tensor, A_scale: torch.Tensor, B: torch.Tensor, B_scale: 
 
 def int4_linear_w4a4(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                      rotation_group: int = 0) -> torch.Tensor:
-    """The reference's own ``int4_linear`` numerics (ops.py:167-183): the
+    """The reference's own ``int4_linear`` (ops.py:167-183), bit for bit: the
     activation is quantized to int4 per 32-block with ``quantize_int4``
-    (bit-exact with the reference's quantizer, int4_gemm_scaled.hip:197-220)
-    before the GEMM. The codes are dequantized exactly to bf16 (one rounding of
-    code * scale) and multiplied with the bf16 weights on the W4A16 path, so
-    the result equals the reference's integer-block GEMM up to those two bf16
-    roundings, not bit for bit."""
+    (int4_gemm_scaled.hip:197-220) and multiplied with the packed weights by
+    the integer-exact ``gemm_int4`` (default split plan), bias in x.dtype."""
     shape = x.shape
     K = shape[-1]
     x2d = x.reshape(-1, K)
     if rotation_group:
         x2d = hadamard_rotate(x2d, rotation_group, torch.float32)  # fp32, as the reference quantizes
     pa, sa = quantize_int4(x2d.contiguous())
-    xq = dequantize_int4(pa, sa, torch.bfloat16)
-    out = gemm_w4a16(xq, w_packed, w_scale, bias, x.dtype)
+    out = gemm_int4(pa, sa, w_packed, w_scale.float(), bias, x.dtype)
     return out.reshape(*shape[:-1], w_packed.shape[0])
 
 
@@ -632,11 +665,11 @@ class Gfx906Int4Ops(_OpsBase):
                 return torch.nn.functional.linear(x, self.weight.to(x.device, x.dtype), bias)
             weight_q4 = self.weight_q4.to(x.device)
             weight_scale = self.weight_scale.to(x.device)
+            bias = self.bias.to(x.device, x.dtype) if self.bias is not None else None
+            if self.activation_quant:  # the integer-exact GEMM takes the fp32 scales
+                return int4_linear_w4a4(x, weight_q4, weight_scale, bias, self.rotation_group)
             if weight_scale is self.weight_scale:
                 weight_scale = self._device_scale(weight_scale)
-            bias = self.bias.to(x.device, x.dtype) if self.bias is not None else None
-            if self.activation_quant:
-                return int4_linear_w4a4(x, weight_q4, weight_scale, bias, self.rotation_group)
             return int4_linear(x, weight_q4, weight_scale, bias, self.rotation_group)
 
 

@@ -127,6 +127,31 @@ int w4a16_gemm_qblock(const void* x, int x_dtype, const void* w_q4, const void* 
                       size_t workspace_bytes, gfx_stream_t stream);
 
 /*
+ * Integer-exact W4A4 GEMM: replaces gemm_int4 (binding.cpp:73-112) with the
+ * reference's numerics bit for bit -- int4_gemm_kernel's per-block chain
+ * acc = fmaf((float)dot, a_scale * b_scale, acc) over 32-element blocks (two
+ * 16-element halves, low then high, for qblock 16; int4_gemm_scaled.hip:
+ * 147-160), each split-K slice's chain from 0 and the slices summed in order
+ * (splitk_reduce_kernel, :182-191), then + bias, one conversion to out_dtype.
+ * a_q4 [M, K/2] / b_q4 [N, K/2]: packed int4 (quantize_int4 / quantize_pack_int4
+ * layout), 16-byte aligned; a_scale [M, K/qblock] / b_scale [N, K/qblock]
+ * float32 (b_scale 16-byte aligned); bias [N] in out_dtype or NULL; y [M, N]
+ * out_dtype.
+ * splits: 0 = the reference's auto_splits (binding.cpp:36-43) evaluated with
+ * this device's SM count, or 1..8. The split count changes the rounding, as in
+ * the reference; w4a4_gemm_exact_splits reports the count a call would use.
+ * workspace: >= w4a4_gemm_exact_workspace_bytes(M, N, K, qblock) bytes,
+ * 16-byte aligned (e5m2 copies of A, transposed A scales and, when K/qblock
+ * is not a multiple of 4, a padded copy of B_scale; rewritten every call).
+ * Errors as gemm_int4's TORCH_CHECKs (K % 32, qblock, splits, dtypes).
+ */
+size_t w4a4_gemm_exact_workspace_bytes(int M, int N, int K, int qblock);
+int w4a4_gemm_exact_splits(int M, int N, int K, int splits);
+int w4a4_gemm_exact(const void* a_q4, const float* a_scale, const void* b_q4, const float* b_scale, int qblock,
+                    const void* bias, void* y, int out_dtype, int M, int N, int K, int splits, void* workspace,
+                    size_t workspace_bytes, gfx_stream_t stream);
+
+/*
  * W4A16 GEMM that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a plugin host that passes
  * only its input/output device pointers and owns the memory budget, or code
