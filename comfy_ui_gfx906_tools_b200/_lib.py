@@ -59,6 +59,10 @@ SIGNATURES = {
     "w4a16_gemm_qblock": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p]),
     "scales_to_f16": (_c_int, [_c_void_p, _c_void_p, _c_int64, _c_void_p, _c_void_p]),
+    "quantize_int4_rows": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, ctypes.c_uint32, _c_void_p,
+                                    _c_void_p, _c_void_p]),
+    "quantize_int4_cols": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int, ctypes.c_uint32,
+                                    _c_void_p, _c_void_p, _c_void_p]),
     "w4a4_gemm_exact_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "w4a4_gemm_exact_splits": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
     "w4a4_gemm_exact": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,

@@ -349,6 +349,35 @@ int w4a4_gemm_exact(const void* a_q4, const float* a_scale, const void* b_q4, co
                            sm_count(dev));
 }
 
+static int check_train_quant(const char* fn, const void* x, int64_t row_stride, int R, int C, int mult_r, int mult_c,
+                             const void* packed, const void* scale) {
+  if (!x || !packed || !scale) return set_error(GFX_ERR_INVALID, "%s: x, packed and scale must be device pointers", fn);
+  if (R < 0 || C < 0 || R % mult_r != 0 || C % mult_c != 0)
+    return set_error(GFX_ERR_INVALID, "%s: x must be [R %% %d == 0, C %% %d == 0], got [%d, %d]", fn, mult_r, mult_c, R,
+                     C);
+  if (row_stride < C || row_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return set_error(GFX_ERR_INVALID, "%s: x rows must be 16-byte aligned, got row stride %lld", fn,
+                     (long long)row_stride);
+  if ((reinterpret_cast<uintptr_t>(packed) & 15) != 0 || (reinterpret_cast<uintptr_t>(scale) & 7) != 0)
+    return set_error(GFX_ERR_INVALID, "%s: packed must be 16-byte and scale 8-byte aligned", fn);
+  return GFX_OK;
+}
+
+int quantize_int4_rows(const void* x, int64_t row_stride, int R, int C, int sr, uint32_t seed, void* packed,
+                       float* scale, gfx_stream_t stream) {
+  int rc = check_train_quant("quantize_int4_rows", x, row_stride, R, C, 1, 32, packed, scale);
+  if (rc) return rc;
+  return launch_quantize_int4_rows(x, row_stride, R, C, sr, seed, packed, scale, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int quantize_int4_cols(const void* x, int64_t row_stride, int R, int C, const float* signs, int sr, uint32_t seed,
+                       void* packed, float* scale, gfx_stream_t stream) {
+  int rc = check_train_quant("quantize_int4_cols", x, row_stride, R, C, 32, 1, packed, scale);
+  if (rc) return rc;
+  return launch_quantize_int4_cols(x, row_stride, R, C, signs, sr, seed, packed, scale,
+                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
 int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
                          const void* bias, void* const* y_ranks, int n_ranks, int rank, int out_dtype, int M,
                          int N_local, int K, int splits, void* workspace, size_t workspace_bytes,

@@ -64,6 +64,14 @@ int launch_w4a4_exact(const void* a_q4, const float* a_scale, const void* b_q4, 
                       cudaStream_t stream, int sms);
 int w4a4x_device_status(int clear);
 
+// block-16 int4 training quantizers -- train_quant.cu
+// x fp16 [R, C] (rows row_stride elements apart). rows: C % 32 == 0 -> packed [R, C/2], scale [R, C/16].
+// cols: R % 32 == 0 -> packed [C, R/2], scale [C, R/16] (transposed; signs: 16 floats or null).
+int launch_quantize_int4_rows(const void* x, long long row_stride, int R, int C, int sr, uint32_t seed, void* packed,
+                              float* scale, cudaStream_t stream);
+int launch_quantize_int4_cols(const void* x, long long row_stride, int R, int C, const float* signs, int sr,
+                              uint32_t seed, void* packed, float* scale, cudaStream_t stream);
+
 // loaders / helpers -- pack.cu
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
                         cudaStream_t stream, int qblock = 32);

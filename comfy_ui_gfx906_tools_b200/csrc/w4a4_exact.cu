@@ -20,18 +20,22 @@
 // reference) runs on the CUDA cores, in packed f32x2 instructions, in
 // registers that hold the accumulators across the whole K loop.
 //
-// One persistent CTA per SM, 14 warps:
+// One persistent CTA per SM, 20 warps:
 //   warp 0      producer: TMA of the activation tile (e5m2, prepared once per
-//               call by e5m2_prepass_kernel), of the weight nibbles and of
-//               the transposed activation scales, per 128-wide K stage.
+//               call by e5m2_prepass_kernel) and of the weight nibbles per
+//               128-wide K stage (4-stage ring, freed by the MMAs), and of both
+//               operands' scales (8-stage ring, freed by the rescale warps).
 //   warp 1      TMEM allocation; one thread issues one MMA per 32-element
 //               block (M = 128 weight rows, N = the tile's token columns,
 //               K = 32) into one of 4 TMEM slots and commits it.
-//   warps 2-5   unpack: weight nibbles -> e5m2 in the UMMA K-major
+//   warps 2-3   unpack: weight nibbles -> e5m2 in the UMMA K-major
 //               SWIZZLE_128B layout, proxy fence, mbarrier arrive.
-//   warps 6-13  rescale: tcgen05.ld of a slot's dot products, release the
-//               slot, then the fp32 chain for 128 rows x the tile's tokens;
-//               at the end of a tile, + bias, convert, store.
+//   warps 4-19  rescale: four warps per TMEM lane quarter, one column group
+//               each; per block all TMEM reads, one wait, release the slot,
+//               then the fp32 chain. Measured: with one 16-column read in
+//               flight per warp and 8 rescale warps, the TMEM read latency
+//               (not the FMA pipe) set the pace, ~1300 cycles per block.
+//               At the end of a tile: + bias, convert, store.
 // Every mbarrier wait is bounded (common.cuh).
 #include <string.h>
 
@@ -51,10 +55,13 @@ constexpr int kBlocks = 4;        // 32-element blocks per stage
 constexpr int kSlots = 4;         // TMEM slots, one block's dot products each
 constexpr int kStages = 4;         // activation / weight stages (freed by the MMAs)
 constexpr int kSStages = 8;        // scale stages (freed by the rescale warps, which trail the MMAs)
-constexpr int kProducerWarp = 0, kMmaWarp = 1, kUnpackWarp0 = 2, kUnpackWarps = 4, kRescaleWarp0 = 6,
-              kRescaleWarps = 8;
+constexpr int kProducerWarp = 0, kMmaWarp = 1, kUnpackWarp0 = 2, kUnpackWarps = 2, kRescaleWarp0 = 4,
+              kRescaleWarps = 16;
 constexpr int kThreads = (kRescaleWarp0 + kRescaleWarps) * 32;
 constexpr int kSmemLimit = 232448;
+#ifndef GFX_W4A4X_BATCH_MMA
+#define GFX_W4A4X_BATCH_MMA 0
+#endif
 
 // Token tile per template: 128 tokens for 32-element blocks, 64 when the
 // rescale threads also carry the split partial sum or (qblock 16) two
@@ -64,7 +71,7 @@ template <int SUB, bool kSplit>
 struct Cfg {
   static constexpr int kTok = (SUB == 2 || kSplit) ? 64 : 128;
   static constexpr int kCols = SUB == 2 ? 2 * kTok : kTok;  // MMA N = TMEM columns per slot
-  static constexpr int kTPT = kTok / 2;                      // tokens per rescale thread
+  static constexpr int kTPT = kTok / 4;                      // tokens per rescale thread (4 column groups)
   static constexpr int kScalesPerStage = kBlocks * SUB;
   static constexpr int kActBytes = kCols * kStageK;          // e5m2 token rows (MMA B)
   static constexpr int kWBytes = kRows * kStageK;            // e5m2 weight rows (MMA A)
@@ -176,6 +183,22 @@ __global__ void __launch_bounds__(256) scale_pad_kernel(const float* __restrict_
   pdl_trigger();
 }
 
+// The reference's split-K reduction (splitk_reduce_kernel,
+// int4_gemm_scaled.hip:182-191): v = 0; v += partial[s] in slice order; + bias.
+template <typename OutT>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ part, int P,
+                                                           const OutT* __restrict__ bias, OutT* __restrict__ y, int M,
+                                                           int N) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (i < (long)M * N) {
+    float v = 0.0f;
+    for (int s = 0; s < P; ++s) v = __fadd_rn(v, part[(size_t)s * M * N + i]);
+    if (bias != nullptr) v = __fadd_rn(v, to_f32(bias[i % N]));
+    y[i] = from_f32<OutT>(v);
+  }
+}
+
 struct Smem {
   uint8_t* stage0;     // stage s at stage0 + s * kStageBytes: [act e5m2 | W e5m2 | W nibbles]
   uint8_t* scale0;     // scale stage i at scale0 + i * kScaleBytes: [act scales [scale][token] | W scales [row][scale]]
@@ -212,14 +235,20 @@ __device__ __forceinline__ void chain4(float* acc, const uint32_t* d, float4 sa,
   acc[3] = a23.y;
 }
 
-template <typename OutT, int SUB, bool kSplit>
+// kMode 0: one chain per output. 1: the reference's split-K slices run one
+// after another in the CTA (the partial sum in registers). 2: the slices run
+// in parallel as separate work items, each storing its fp32 partial to
+// y[slice][M][N] (no bias); split_reduce_kernel sums them in slice order.
+template <typename OutT, int SUB, int kMode>
 __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constant__ CUtensorMap a_map,
                                                             const __grid_constant__ CUtensorMap a2_map,
                                                             const __grid_constant__ CUtensorMap q_map,
                                                             const __grid_constant__ CUtensorMap s_map,
                                                             const __grid_constant__ CUtensorMap sb_map,
                                                             const OutT* __restrict__ bias, OutT* __restrict__ y,
-                                                            int M, int N, int K, int split_blocks, int* status_host) {
+                                                            int M, int N, int K, int split_blocks, int n_par,
+                                                            int* status_host) {
+  constexpr bool kSplit = kMode == 1, kPar = kMode == 2;
   using T = Cfg<SUB, kSplit>;
   constexpr int kTok = T::kTok, kCols = T::kCols, kTPT = T::kTPT, kSPS = T::kScalesPerStage;
   constexpr int kStageBytes = T::kStageBytes, kActBytes = T::kActBytes, kWBytes = T::kWBytes,
@@ -243,12 +272,18 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int S = K * SUB / 32;          // scales per row
   const int nb = K / 32;               // 32-element blocks per row
-  const int k_stages = (nb + kBlocks - 1) / kBlocks;
   const int tiles_m = (M + kTok - 1) / kTok;
   const int tiles_n = (N + kRows - 1) / kRows;
   const int num_tiles = tiles_m * tiles_n;
+  const int num_items = num_tiles * (kPar ? n_par : 1);  // work items: (tile, slice)
+  // the 32-element blocks [kb0, kb1) and stages [ks0, ks1) of a work item
+  auto item_range = [&](int item, int& kb0, int& kb1, int& ks0, int& ks1) {
+    kb0 = kPar ? (item % n_par) * split_blocks : 0;
+    kb1 = kPar ? (kb0 + split_blocks < nb ? kb0 + split_blocks : nb) : nb;
+    ks0 = kb0 / kBlocks;
+    ks1 = (kb1 + kBlocks - 1) / kBlocks;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -285,9 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
       tma_prefetch_desc(&sb_map);
       pdl_wait();  // the activation copies come from the pre-pass kernels
       uint32_t kit = 0, aissued = 0, sissued = 0;  // stages issued: activation/weight, scales
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        const int tile = kPar ? item / n_par : item;
         const int m0 = (tile % tiles_m) * kTok, n0 = (tile / tiles_m) * kRows;
-        for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+        int kb0, kb1, ks0, ks1;
+        item_range(item, kb0, kb1, ks0, ks1);
+        for (int ks = ks0; ks < ks1; ++ks, ++kit) {
           const int s = kit % kStages;
           const uint32_t ph = (kit / kStages) & 1;
           if (!mbar_wait(&sm.empty[s], ph ^ 1, kDevErrEmptyBarrierTimeout)) { ok = false; break; }
@@ -323,21 +361,23 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
   } else if (warp >= kUnpackWarp0 && warp < kUnpackWarp0 + kUnpackWarps) {
     // --------------------------------- unpack ---------------------------------
     // Lane l takes the 32-element block l & 3 of rows 8i + (l >> 2) of the
-    // warp's 32 rows: the warp reads 512 contiguous nibble bytes per step and
+    // warp's 64 rows: the warp reads 512 contiguous nibble bytes per step and
     // its 16-byte stores fall on 8 distinct bank groups per 8 lanes.
     const int u = warp - kUnpackWarp0;
     const int c = lane & 3;
     uint32_t kit = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int ks = 0; ks < k_stages; ++ks, ++kit) {
+    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      int kb0, kb1, ks0, ks1;
+      item_range(item, kb0, kb1, ks0, ks1);
+      for (int ks = ks0; ks < ks1; ++ks, ++kit) {
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
         if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout)) { ok = false; break; }
         const uint32_t wa = smem_u32(sm.stage0 + s * kStageBytes + kActBytes);
         const uint32_t qa = wa + kWBytes;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = 32 * u + 8 * i + (lane >> 2);
+        for (int i = 0; i < kRows / kUnpackWarps / 8; ++i) {
+          const int r = kRows / kUnpackWarps * u + 8 * i + (lane >> 2);
           uint4 lo, hi;
           block_to_e5m2(lds128(qa + r * (kStageK / 2) + c * 16), lo, hi);
           const uint32_t row = wa + (r >> 3) * 1024 + (r & 7) * 128;
@@ -353,8 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
     // ---------------------------------- MMA -----------------------------------
     constexpr uint32_t kId = idesc_e5m2<kCols>();
     uint32_t kit = 0, bit = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int ks = 0; ks < k_stages && ok; ++ks, ++kit) {
+    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      int kb0, kb1, ks0, ks1;
+      item_range(item, kb0, kb1, ks0, ks1);
+      for (int ks = ks0; ks < ks1 && ok; ++ks, ++kit) {
         const int s = kit % kStages;
         const uint32_t ph = (kit / kStages) & 1;
         if (!mbar_wait(&sm.full[s], ph, kDevErrFullBarrierTimeout) ||
@@ -365,7 +407,26 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
         tc::tc_fence_after();
         const uint32_t xa = smem_u32(sm.stage0 + s * kStageBytes);
         const uint64_t adesc = tc::sw128_desc(xa + kActBytes), bdesc = tc::sw128_desc(xa);
-        const int nblk = nb - ks * kBlocks < kBlocks ? nb - ks * kBlocks : kBlocks;
+        const int nblk = kb1 - ks * kBlocks < kBlocks ? kb1 - ks * kBlocks : kBlocks;
+#if GFX_W4A4X_BATCH_MMA
+        // every slot of the stage free first, then the stage's MMAs back to back
+        for (int j = 0; j < nblk && ok; ++j) {
+          const uint32_t b = bit + j;
+          if (!mbar_wait(&sm.dempty[b % kSlots], ((b / kSlots) & 1) ^ 1, kDevErrMmaBarrierTimeout)) ok = false;
+        }
+        if (!ok) break;
+        tc::tc_fence_after();
+        if (lane == 0) {
+          for (int j = 0; j < nblk; ++j) {
+            const int slot = (bit + j) % kSlots;
+            tc::umma_f8f6f4(tmem + slot * kCols, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), kId, 0u);
+            tc::umma_commit<1>(&sm.dfull[slot]);
+          }
+          tc::umma_commit<1>(&sm.empty[s]);
+        }
+        __syncwarp();
+        bit += nblk;
+#else
         for (int j = 0; j < nblk; ++j, ++bit) {
           const int slot = bit % kSlots;
           if (!mbar_wait(&sm.dempty[slot], ((bit / kSlots) & 1) ^ 1, kDevErrMmaBarrierTimeout)) {
@@ -382,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
           }
           __syncwarp();
         }
+#endif
       }
     }
     if (lane == 0) tc::umma_commit<1>(sm.drain);
@@ -389,42 +451,34 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
     if (!mbar_wait(sm.drain, 0, kDevErrMmaBarrierTimeout)) ok = false;
   } else {
     // -------------------------------- rescale ---------------------------------
-    // Each thread owns one weight row (its TMEM lane) and kTPT token columns.
-    // The dot products of a block are read 16 columns at a time, and the read
-    // of the next 16 (the next block's first 16 after the last) is in flight
-    // while the current 16 go through the chain.
+    // Each thread owns one weight row (its TMEM lane) and kTPT token columns;
+    // the four warps on one SM sub-partition own the four column groups of one
+    // lane quarter. Per block a warp issues all its TMEM reads, waits once,
+    // releases the slot and runs the chain; the sub-partition's other warps
+    // cover the read latency.
     pdl_wait();  // bias and y only after the previous kernel of the stream
-    const int q = warp & 3;                        // TMEM lanes 32q .. 32q + 31 (this warp's quarter)
-    const int t0 = ((warp - kRescaleWarp0) >> 2) * kTPT;  // first token column of this thread
-    constexpr int kNCh = kTPT / 16;                // 16-column chunks per block half
-    constexpr int kMaxChunks = kNCh * SUB;         // SUB 2: chunk c = tokens 16 (c / 2), half c % 2
+    const int q = warp & 3;                                      // TMEM lanes 32q .. 32q + 31
+    const int t0 = ((warp - kRescaleWarp0) >> 2) * kTPT;         // first token column of this thread
+    constexpr int kNCh = kTPT / 16;                              // 16-column chunks per block half
+    constexpr int kMaxChunks = kNCh * SUB;                       // SUB 2: chunk c = tokens 16 (c / 2), half c % 2
     uint32_t kit = 0, bit = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      const int tile = kPar ? item / n_par : item;
+      int kb0, kb1, ks0, ks1;
+      item_range(item, kb0, kb1, ks0, ks1);
       const int m0 = (tile % tiles_m) * kTok, n0 = (tile / tiles_m) * kRows;
       const int n = n0 + 32 * q + lane;
       const int live_tok = M - m0 - t0;  // tokens of this thread's columns inside M (may be <= 0)
-      // chunks holding tokens < M, an even count (a chunk past M only adds zeros
-      // to accumulators that are never stored)
       int nlive = live_tok <= 0 ? 0 : (live_tok + 15) / 16;
       if (nlive > kNCh) nlive = kNCh;
-      const int nch = SUB == 2 ? 2 * nlive : (nlive + 1) & ~1;
+      const int nch = nlive * SUB;  // chunks holding tokens < M
       float acc[kTPT], tot[kSplit ? kTPT : 1];
 #pragma unroll
       for (int i = 0; i < kTPT; ++i) acc[i] = 0.0f;
 #pragma unroll
       for (int i = 0; i < (kSplit ? kTPT : 1); ++i) tot[i] = 0.0f;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-      auto chunk_col = [&](int c) { return SUB == 1 ? t0 + 16 * c : (c & 1) * kTok + t0 + 16 * (c >> 1); };
-      uint32_t d[2][16];
-      // the tile's first block
-      {
-        const int slot = bit % kSlots;
-        if (!mbar_wait(&sm.dfull[slot], (bit / kSlots) & 1, kDevErrEpilogueBarrierTimeout)) { ok = false; break; }
-        tc::tc_fence_after();
-        if (nch > 0) tc::tmem_ld16_nowait(lane_base + slot * kCols + chunk_col(0), d[0]);
-        tc::tmem_wait_ld();
-      }
-      for (int kb = 0; kb < nb && ok; ++kb, ++bit) {
+      for (int kb = kb0; kb < kb1 && ok; ++kb, ++bit) {
         const int j = kb % kBlocks;
         const int si = kit % kSStages;
         if (j == 0) {
@@ -432,6 +486,21 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
           if (!mbar_wait(&sm.sfull[si], (kit / kSStages) & 1, kDevErrFullBarrierTimeout)) { ok = false; break; }
         }
         const uint32_t sa_base = smem_u32(sm.scale0 + si * T::kScaleBytes);
+        const int slot = bit % kSlots;
+        if (!mbar_wait(&sm.dfull[slot], (bit / kSlots) & 1, kDevErrEpilogueBarrierTimeout)) { ok = false; break; }
+        tc::tc_fence_after();
+        uint32_t d[kMaxChunks][16];
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+          const int col = SUB == 1 ? t0 + 16 * c : (c & 1) * kTok + t0 + 16 * (c >> 1);
+          if (c < nch) tc::tmem_ld16_nowait(lane_base + slot * kCols + col, d[c]);
+        }
+        float sbv[SUB];  // this row's weight scales for the block (zero past N or K)
+        {
+          const uint32_t a = sa_base + T::kSaBytes + (uint32_t)(((32 * q + lane) * kSPS + SUB * j) * 4);
+          sbv[0] = lds_f32(a);
+          if (SUB == 2) sbv[SUB - 1] = lds_f32(a + 4);
+        }
         if constexpr (kSplit) {
           if (kb > 0 && kb % split_blocks == 0) {  // a new split's chain starts at 0
 #pragma unroll
@@ -441,53 +510,22 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
             }
           }
         }
-        float sbv[SUB];  // this row's weight scales for the block (zero past N or K)
-        {
-          const uint32_t a = sa_base + T::kSaBytes + (uint32_t)(((32 * q + lane) * kSPS + SUB * j) * 4);
-          sbv[0] = lds_f32(a);
-          if (SUB == 2) sbv[SUB - 1] = lds_f32(a + 4);
-        }
-        const int slot = bit % kSlots;
-        const bool more = kb + 1 < nb;
-        const int nslot = (bit + 1) % kSlots;
-        auto release_and_prefetch = [&]() {
-          // every read of this block's slot has completed (the last tmem_wait_ld)
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.dempty[slot]);
-          if (more) {
-            if (!mbar_wait(&sm.dfull[nslot], ((bit + 1) / kSlots) & 1, kDevErrEpilogueBarrierTimeout)) {
-              ok = false;
-              return false;
-            }
-            tc::tc_fence_after();
-            if (nch > 0) tc::tmem_ld16_nowait(lane_base + nslot * kCols + chunk_col(0), d[0]);
-          }
-          return true;
-        };
-        if (nch == 0) {
-          if (!release_and_prefetch()) break;
-        }
+        tc::tmem_wait_ld();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.dempty[slot]);
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c) {
           if (c < nch) {
-            if (c + 1 < nch) {
-              tc::tmem_ld16_nowait(lane_base + slot * kCols + chunk_col(c + 1), d[(c + 1) & 1]);
-            } else if (!release_and_prefetch()) {
-              break;
-            }
-            const int tc0 = SUB == 1 ? 16 * c : 16 * (c >> 1);  // first token of the chunk (thread-relative)
+            const int tc0 = SUB == 1 ? 16 * c : 16 * (c >> 1);     // first token of the chunk (thread-relative)
             const int sidx = SUB * j + (SUB == 2 ? (c & 1) : 0);  // scale index within the stage
             const float sb = sbv[SUB == 2 ? (c & 1) : 0];
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
-              chain4(acc + tc0 + i, d[c & 1] + i, lds_f32x4(sa_base + (uint32_t)((sidx * kTok + t0 + tc0 + i) * 4)),
-                     sb);
-            tc::tmem_wait_ld();
+              chain4(acc + tc0 + i, d[c] + i, lds_f32x4(sa_base + (uint32_t)((sidx * kTok + t0 + tc0 + i) * 4)), sb);
           }
         }
-        if (!ok) break;
-        if (j == kBlocks - 1 || !more) {
+        if (j == kBlocks - 1 || kb + 1 == kb1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.sempty[si]);
           ++kit;
@@ -495,15 +533,24 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
       }
       if (!ok) break;
       if (n < N) {
-        const float b = bias != nullptr ? to_f32(bias[n]) : 0.0f;
+        if constexpr (kPar) {
+          float* part = reinterpret_cast<float*>(y) + (size_t)(item % n_par) * M * N;
 #pragma unroll
-        for (int i = 0; i < kTPT; ++i) {
-          const int m = m0 + t0 + i;
-          if (m < M) {
-            float v = acc[i];
-            if constexpr (kSplit) v = __fadd_rn(tot[i], acc[i]);
-            if (bias != nullptr) v = __fadd_rn(v, b);
-            y[(size_t)m * N + n] = from_f32<OutT>(v);
+          for (int i = 0; i < kTPT; ++i) {
+            const int m = m0 + t0 + i;
+            if (m < M) part[(size_t)m * N + n] = acc[i];
+          }
+        } else {
+          const float b = bias != nullptr ? to_f32(bias[n]) : 0.0f;
+#pragma unroll
+          for (int i = 0; i < kTPT; ++i) {
+            const int m = m0 + t0 + i;
+            if (m < M) {
+              float v = acc[i];
+              if constexpr (kSplit) v = __fadd_rn(tot[i], acc[i]);
+              if (bias != nullptr) v = __fadd_rn(v, b);
+              y[(size_t)m * N + n] = from_f32<OutT>(v);
+            }
           }
         }
       }
@@ -543,10 +590,10 @@ int reference_auto_splits(int M, int N, int K, int sms) {
   return wanted < max_splits ? wanted : max_splits;
 }
 
-template <typename OutT, int SUB, bool kSplit>
+template <typename OutT, int SUB, int kMode>
 int launch_kernel(const void* a8, const float* sat, const void* b_q4, const float* b_scale, const void* bias, void* y,
-                  int M, int N, int K, int Mp, int Sp, int split_blocks, cudaStream_t st, int sms) {
-  using T = w4a4x::Cfg<SUB, kSplit>;
+                  int M, int N, int K, int Mp, int Sp, int split_blocks, int n_par, cudaStream_t st, int sms) {
+  using T = w4a4x::Cfg<SUB, kMode == 1>;
   const int S = K * SUB / 32;
   CUtensorMap am, am2, qm, smap;
   int rc = cached_tmap_2d(&am, CU_TENSOR_MAP_DATA_TYPE_UINT8, a8, (uint64_t)K, (uint64_t)M, (uint64_t)K,
@@ -570,7 +617,7 @@ int launch_kernel(const void* a8, const float* sat, const void* b_q4, const floa
   rc = cached_tmap_2d(&sbm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, b_scale, (uint64_t)S, (uint64_t)N, (uint64_t)Sp * 4,
                       T::kScalesPerStage, w4a4x::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  auto kern = w4a4x::w4a4x_kernel<OutT, SUB, kSplit>;
+  auto kern = w4a4x::w4a4x_kernel<OutT, SUB, kMode>;
   static bool attr_set[64] = {false};
   const int dev = current_device();
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -580,7 +627,7 @@ int launch_kernel(const void* a8, const float* sat, const void* b_q4, const floa
                        cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const int tiles = ((M + T::kTok - 1) / T::kTok) * ((N + w4a4x::kRows - 1) / w4a4x::kRows);
+  const int tiles = ((M + T::kTok - 1) / T::kTok) * ((N + w4a4x::kRows - 1) / w4a4x::kRows) * n_par;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(tiles < sms ? tiles : sms);
@@ -592,26 +639,54 @@ int launch_kernel(const void* a8, const float* sat, const void* b_q4, const floa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, am, am2, qm, smap, sbm, (const OutT*)bias, (OutT*)y, M, N, K,
-                                     split_blocks, host_status_word(dev));
+                                     split_blocks, n_par, host_status_word(dev));
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "w4a4x_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("w4a4x_kernel");
 }
 
-template <int SUB, bool kSplit>
+template <int SUB, int kMode>
 int launch_out(int out_dtype, const void* a8, const float* sat, const void* b_q4, const float* b_scale,
-               const void* bias, void* y, int M, int N, int K, int Mp, int Sp, int split_blocks, cudaStream_t st,
-               int sms) {
-  if (out_dtype == GFX_DTYPE_F32)
-    return launch_kernel<float, SUB, kSplit>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks, st, sms);
-  if (out_dtype == GFX_DTYPE_F16)
-    return launch_kernel<__half, SUB, kSplit>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks, st,
-                                              sms);
-  return launch_kernel<__nv_bfloat16, SUB, kSplit>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks,
-                                                   st, sms);
+               const void* bias, void* y, int M, int N, int K, int Mp, int Sp, int split_blocks, int n_par,
+               cudaStream_t st, int sms) {
+  if constexpr (kMode == 2) {  // slice partials are fp32
+    return launch_kernel<float, SUB, 2>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks, n_par, st,
+                                        sms);
+  } else {
+    if (out_dtype == GFX_DTYPE_F32)
+      return launch_kernel<float, SUB, kMode>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks, n_par,
+                                              st, sms);
+    if (out_dtype == GFX_DTYPE_F16)
+      return launch_kernel<__half, SUB, kMode>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks, n_par,
+                                               st, sms);
+    return launch_kernel<__nv_bfloat16, SUB, kMode>(a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, split_blocks,
+                                                    n_par, st, sms);
+  }
 }
 
+template <typename OutT>
+int launch_reduce(const float* part, int P, const void* bias, void* y, int M, int N, cudaStream_t st) {
+  const long n = (long)M * N;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, w4a4x::split_reduce_kernel<OutT>, part, P, (const OutT*)bias, (OutT*)y, M,
+                                     N);
+  if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "split_reduce_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("split_reduce_kernel");
+}
+
+// Partial sums of parallel slices are kept when all 8 possible slices fit in this many bytes.
+constexpr size_t kMaxPartialBytes = 64ull << 20;
+
 struct Layout {
-  size_t a8, sat, sbp, total;  // byte offsets of the e5m2 A copies, transposed A scales, padded B scales
+  // byte offsets: e5m2 A copies, transposed A scales, padded B scales, slice partials
+  size_t a8, sat, sbp, part, total;
 };
 
 Layout workspace_layout(int M, int N, int K, int qblock, bool pad_b) {
@@ -621,7 +696,9 @@ Layout workspace_layout(int M, int N, int K, int qblock, bool pad_b) {
   l.a8 = 0;
   l.sat = align_up((size_t)sub * M * K, 1024);
   l.sbp = align_up(l.sat + S * Mp * 4, 1024);
-  l.total = l.sbp + (pad_b ? (size_t)N * Sp * 4 : 0);
+  l.part = align_up(l.sbp + (pad_b ? (size_t)N * Sp * 4 : 0), 1024);
+  const size_t part_bytes = (size_t)8 * M * N * 4;
+  l.total = l.part + (part_bytes <= kMaxPartialBytes ? part_bytes : 0);
   return l;
 }
 
@@ -631,7 +708,7 @@ size_t w4a4_exact_workspace(int M, int N, int K, int qblock) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int S = K * (qblock == 16 ? 2 : 1) / 32;
   // the padded weight-scale copy is sized in whenever it may be needed
-  return workspace_layout(M, N, K, qblock, S % 4 != 0).total + 16;
+  return workspace_layout(M, N, K, qblock, S % 4 != 0).total;
 }
 
 int w4a4_exact_splits(int M, int N, int K, int splits, int sms) {
@@ -676,12 +753,25 @@ int launch_w4a4_exact(const void* a_q4, const float* a_scale, const void* b_q4, 
   const int tps = (k_tiles + splits - 1) / splits;
   if (splits > 1 && tps < k_tiles) {
     const int sb = tps * w4a4x::kBlocks;
+    const int n_par = (k_tiles + tps - 1) / tps;  // non-empty slices (an empty one adds +0.0: nothing)
+    if (lay.total - lay.part >= (size_t)n_par * M * N * 4) {
+      // small problems: slices as parallel work items, then the ordered reduction
+      float* part = reinterpret_cast<float*>(base + lay.part);
+      rc = sub == 1 ? launch_out<1, 2>(out_dtype, a8, sat, b_q4, b_scale, nullptr, part, M, N, K, Mp, Sp, sb, n_par,
+                                       st, sms)
+                    : launch_out<2, 2>(out_dtype, a8, sat, b_q4, b_scale, nullptr, part, M, N, K, Mp, Sp, sb, n_par,
+                                       st, sms);
+      if (rc) return rc;
+      if (out_dtype == GFX_DTYPE_F32) return launch_reduce<float>(part, n_par, bias, y, M, N, st);
+      if (out_dtype == GFX_DTYPE_F16) return launch_reduce<__half>(part, n_par, bias, y, M, N, st);
+      return launch_reduce<__nv_bfloat16>(part, n_par, bias, y, M, N, st);
+    }
     if (sub == 1)
-      return launch_out<1, true>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, sb, st, sms);
-    return launch_out<2, true>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, sb, st, sms);
+      return launch_out<1, 1>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, sb, 1, st, sms);
+    return launch_out<2, 1>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, sb, 1, st, sms);
   }
-  if (sub == 1) return launch_out<1, false>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, 0, st, sms);
-  return launch_out<2, false>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, 0, st, sms);
+  if (sub == 1) return launch_out<1, 0>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, 0, 1, st, sms);
+  return launch_out<2, 0>(out_dtype, a8, sat, b_q4, b_scale, bias, y, M, N, K, Mp, Sp, 0, 1, st, sms);
 }
 
 }  // namespace gfx

@@ -459,6 +459,52 @@ def quantize_int4(x: torch.Tensor):
     return quantize_pack_int4(x)
 
 
+def _check_train_quant_input(x: torch.Tensor, mult_r: int, mult_c: int):
+    """binding.cpp:317-327's checks, same substance."""
+    if not (x.is_cuda and x.dtype == torch.float16 and x.dim() == 2 and x.stride(1) == 1):
+        raise RuntimeError(f"x must be a device fp16 [R, C] tensor with contiguous rows, got {x.dtype} "
+                           f"{tuple(x.shape)} strides {tuple(x.stride())}")
+    if x.shape[0] % mult_r != 0 or x.shape[1] % mult_c != 0:
+        raise RuntimeError(f"x must be [R % {mult_r} == 0, C % {mult_c} == 0], got {tuple(x.shape)}")
+    if x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
+        raise RuntimeError(f"x rows must be 16-byte aligned, got row stride {x.stride(0)}")
+
+
+def quantize_int4_rows(x: torch.Tensor, sr: bool, seed: int):
+    """Block-16 int4 quantize along rows for the int4 training GEMMs
+    (``ext.quantize_int4_rows``, binding.cpp:329-339, int4_train_quant.hip:59-85):
+    x fp16 [R, C] (C % 32 == 0) -> (packed int8 [R, C/2], scale float32 [R, C/16]),
+    round to nearest even, or stochastic rounding keyed by ``seed``."""
+    _check_train_quant_input(x, 1, 32)
+    R, C = x.shape
+    packed = torch.empty(R, C // 2, dtype=torch.int8, device=x.device)
+    scale = torch.empty(R, C // 16, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("quantize_int4_rows", x.data_ptr(), x.stride(0), R, C, 1 if sr else 0, int(seed) & 0xFFFFFFFF,
+                  packed.data_ptr(), scale.data_ptr(), _stream(x.device))
+    return packed, scale
+
+
+def quantize_int4_cols(x: torch.Tensor, signs: torch.Tensor | None, sr: bool, seed: int):
+    """Block-16 int4 quantize along columns, transposed (``ext.quantize_int4_cols``,
+    binding.cpp:341-356, int4_train_quant.hip:87-123): x fp16 [R, C] (R % 32 == 0)
+    -> (packed int8 [C, R/2], scale float32 [C, R/16]); with ``signs`` (16 fp32
+    on the device) every 16-row group is first rotated by (H16 / 4) diag(signs)."""
+    _check_train_quant_input(x, 32, 1)
+    if signs is not None and not (signs.is_cuda and signs.dtype == torch.float32 and signs.numel() == 16
+                                  and signs.is_contiguous()):
+        raise RuntimeError(f"signs must be a contiguous device fp32 tensor of 16, got {signs.dtype} "
+                           f"{tuple(signs.shape)}")
+    R, C = x.shape
+    packed = torch.empty(C, R // 2, dtype=torch.int8, device=x.device)
+    scale = torch.empty(C, R // 16, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("quantize_int4_cols", x.data_ptr(), x.stride(0), R, C,
+                  signs.data_ptr() if signs is not None else None, 1 if sr else 0, int(seed) & 0xFFFFFFFF,
+                  packed.data_ptr(), scale.data_ptr(), _stream(x.device))
+    return packed, scale
+
+
 def int4_linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
                 rotation_group: int = 0) -> torch.Tensor:
     """x [..., K] float, packed weights from quantize_pack_int4 (folded through

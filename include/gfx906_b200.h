@@ -152,6 +152,25 @@ int w4a4_gemm_exact(const void* a_q4, const float* a_scale, const void* b_q4, co
                     size_t workspace_bytes, gfx_stream_t stream);
 
 /*
+ * Block-16 int4 quantizers of the int4 training backward (quantize_int4_rows /
+ * quantize_int4_cols, binding.cpp:317-356; int4_train_quant.hip:35-123), in
+ * the layout w4a4_gemm_exact(qblock = 16) reads. x: fp16 [R, C], rows
+ * row_stride elements apart (a multiple of 8, 16-byte aligned rows).
+ * scale = max(amax, 1e-8) * (1/7), code = clamp(round(v / scale), -8, 7) with
+ * round to nearest even (sr = 0) or floor(v / scale + u) (sr != 0), u a
+ * counter-based hash of (seed, element index) in [0, 1) with 24 bits.
+ * rows: blocks of 16 along each row, C % 32 == 0 -> packed int8 [R, C/2],
+ *       scale float32 [R, C/16].
+ * cols: blocks of 16 along each column, transposed: R % 32 == 0 -> packed
+ *       int8 [C, R/2], scale float32 [C, R/16]; with signs (16 floats, else
+ *       NULL) each 16-row group is first rotated by (H16 / 4) diag(signs).
+ */
+int quantize_int4_rows(const void* x, int64_t row_stride, int R, int C, int sr, uint32_t seed, void* packed,
+                       float* scale, gfx_stream_t stream);
+int quantize_int4_cols(const void* x, int64_t row_stride, int R, int C, const float* signs, int sr, uint32_t seed,
+                       void* packed, float* scale, gfx_stream_t stream);
+
+/*
  * W4A16 GEMM that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a plugin host that passes
  * only its input/output device pointers and owns the memory budget, or code

@@ -22,7 +22,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 LIB = os.path.join(OUT_DIR, "libgfx906_ref.so")
 DEFAULT_REF = "/root/reference"
-SOURCES = ("nodes/ComfyUI-Gfx906Int4/csrc/int4_gemm_scaled.hip", "nodes/ComfyUI-Gfx906Int4/csrc/int8_gemm.hip")
+SOURCES = ("nodes/ComfyUI-Gfx906Int4/csrc/int4_gemm_scaled.hip", "nodes/ComfyUI-Gfx906Int4/csrc/int8_gemm.hip",
+           "nodes/ComfyUI-Gfx906Int4/csrc/int4_train_quant.hip")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-Xcompiler", "-fPIC",
          "-I", os.path.join(HERE, "hip_shim")]
 

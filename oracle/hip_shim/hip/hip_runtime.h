@@ -1,6 +1,6 @@
 /* Stand-in for the HIP runtime header, so that the reference's own HIP
  * kernel sources (nodes/ComfyUI-Gfx906Int4/csrc/int4_gemm_scaled.hip,
- * int8_gemm.hip) compile unmodified with nvcc as CUDA for the B200, as a
+ * int8_gemm.hip, int4_train_quant.hip) compile unmodified with nvcc as CUDA for the B200, as a
  * test oracle. It maps the few HIP names those files use onto CUDA and
  * restates the two gfx906 dot-product builtins they call from the ISA's
  * definition. TEST INFRASTRUCTURE ONLY: nothing of the product links it. */
@@ -32,3 +32,15 @@ __device__ __forceinline__ int gfx906_ref_sdot4(int a, int b, int c, bool) { ret
 
 #define __builtin_amdgcn_sdot8(a, b, c, clamp) gfx906_ref_sdot8((a), (b), (c), (clamp))
 #define __builtin_amdgcn_sdot4(a, b, c, clamp) gfx906_ref_sdot4((a), (b), (c), (clamp))
+
+/* clang's __builtin_bit_cast on CUDA's __half2, which nvcc rejects as not
+ * trivially copyable: the same bit copy through memcpy. */
+#include <cstring>
+template <typename To, typename From>
+__host__ __device__ __forceinline__ To gfx906_ref_bit_cast(const From& f) {
+  static_assert(sizeof(To) == sizeof(From), "bit cast between types of different sizes");
+  To t;
+  memcpy(&t, &f, sizeof(To));
+  return t;
+}
+#define __builtin_bit_cast(T, v) gfx906_ref_bit_cast<T>(v)

@@ -40,7 +40,8 @@ __all__ = [
     "quantize_dequantize_int4", "build_q4_0_bytes", "w4a16_matmul", "quantize_int8",
     "dequant_int8", "w8a16_matmul", "parity_metrics", "unpack_int4_codes", "pack_int4_codes",
     "torch_cpu_dequant", "torch_cpu_w4a16", "w4a16_matmul_bf16w", "w4a4_matmul", "block_int_matmul",
-    "build_q8_0_bytes", "repack_q8_0",
+    "build_q8_0_bytes", "repack_q8_0", "lowbias32", "hash_uniform", "quant_block16", "quantize_int4_rows",
+    "quantize_int4_cols", "hadamard16",
 ]
 
 
@@ -362,3 +363,89 @@ def parity_metrics(got: np.ndarray, ref: np.ndarray) -> dict:
         "mean_rel": float(d.mean()) / mean_ref if mean_ref > 0 else float(d.mean() if d.size else 0.0),
         "nonfinite": int((~np.isfinite(g)).sum()),
     }
+
+
+# ---------------------------------------------------------------------------
+# block-16 training quantizers (int4_train_quant.hip:16-123)
+# ---------------------------------------------------------------------------
+def lowbias32(x: np.ndarray) -> np.ndarray:
+    """Chris Wellons' lowbias32 integer hash (the counter-based hash of
+    int4_train_quant.hip:18-25), elementwise on uint32."""
+    x = np.asarray(x, dtype=np.uint32).copy()
+    x ^= x >> np.uint32(16)
+    x = (x.astype(np.uint64) * 0x7FEB352D).astype(np.uint32)
+    x ^= x >> np.uint32(15)
+    x = (x.astype(np.uint64) * 0x846CA68B).astype(np.uint32)
+    x ^= x >> np.uint32(16)
+    return x
+
+
+def hash_uniform(seed: int, element: np.ndarray) -> np.ndarray:
+    """u in [0, 1) with 24 bits per (seed, 64-bit element index)
+    (int4_train_quant.hip:27-31)."""
+    e = np.asarray(element, dtype=np.uint64)
+    inner = lowbias32((e & np.uint64(0xFFFFFFFF)).astype(np.uint32) ^ lowbias32((e >> np.uint64(32)).astype(np.uint32)))
+    h = lowbias32(np.uint32(seed & 0xFFFFFFFF) ^ inner)
+    return ((h >> np.uint32(8)).astype(np.float32) * np.float32(1.0 / 16777216.0)).astype(np.float32)
+
+
+def quant_block16(v: np.ndarray, sr: bool, seed: int, first: np.ndarray):
+    """16 values per row of v [B, 16] -> (codes int [B, 16], scale float32 [B])
+    (int4_train_quant.hip:33-55): scale = max(amax, 1e-8) * (1/7) in fp32,
+    t = v / scale, round half even or floor(t + u), clamp to [-8, 7]."""
+    v = np.asarray(v, dtype=np.float32)
+    amax = np.max(np.abs(v), axis=1)
+    s = (np.maximum(amax, np.float32(1e-8)) * np.float32(1.0 / 7.0)).astype(np.float32)
+    t = (v / s[:, None]).astype(np.float32)
+    if sr:
+        u = hash_uniform(seed, np.asarray(first, dtype=np.uint64)[:, None] + np.arange(16, dtype=np.uint64)[None, :])
+        r = np.floor((t + u).astype(np.float32))
+    else:
+        r = np.rint(t)
+    return np.clip(r, -8, 7).astype(np.int64), s
+
+
+def hadamard16(v: np.ndarray, signs: np.ndarray) -> np.ndarray:
+    """(H16 / 4) diag(signs) v for every row of v [B, 16]: four stages of
+    fp32 pair sums / differences in the reference's order
+    (int4_train_quant.hip:103-116)."""
+    v = (np.asarray(v, dtype=np.float32) * np.asarray(signs, dtype=np.float32)[None, :]).astype(np.float32)
+    h = 1
+    while h < 16:
+        v = v.copy()
+        for i in range(16):
+            if i & h == 0:
+                a, b = v[:, i].copy(), v[:, i + h].copy()
+                v[:, i] = (a + b).astype(np.float32)
+                v[:, i + h] = (a - b).astype(np.float32)
+        h <<= 1
+    return (v * np.float32(0.25)).astype(np.float32)
+
+
+def quantize_int4_rows(x: np.ndarray, sr: bool = False, seed: int = 0):
+    """x [R, C] (fp16 values, C % 32 == 0) -> (packed int8 [R, C/2], scale
+    float32 [R, C/16]), blocks of 16 along each row (quant_rows_b16,
+    int4_train_quant.hip:57-85; element index r * C + column)."""
+    x = np.asarray(x, dtype=np.float32)
+    R, C = x.shape
+    v = x.reshape(R * C // 16, 16)
+    first = (np.arange(R, dtype=np.uint64)[:, None] * np.uint64(C) +
+             np.arange(0, C, 16, dtype=np.uint64)[None, :]).reshape(-1)
+    codes, s = quant_block16(v, sr, seed, first)
+    return pack_int4_codes(codes.reshape(R, C)), s.reshape(R, C // 16)
+
+
+def quantize_int4_cols(x: np.ndarray, signs=None, sr: bool = False, seed: int = 0):
+    """x [R, C] (fp16 values, R % 32 == 0) -> (packed int8 [C, R/2], scale
+    float32 [C, R/16]), blocks of 16 along each column of x, i.e. rows of x^T,
+    optionally rotated by hadamard16 first (quant_cols_b16,
+    int4_train_quant.hip:87-123; element index c * R + row)."""
+    xt = np.ascontiguousarray(np.asarray(x, dtype=np.float32).T)  # [C, R]
+    C, R = xt.shape
+    v = xt.reshape(C * R // 16, 16)
+    if signs is not None:
+        v = hadamard16(v, signs)
+    first = (np.arange(C, dtype=np.uint64)[:, None] * np.uint64(R) +
+             np.arange(0, R, 16, dtype=np.uint64)[None, :]).reshape(-1)
+    codes, s = quant_block16(v, sr, seed, first)
+    return pack_int4_codes(codes.reshape(C, R)), s.reshape(C, R // 16)

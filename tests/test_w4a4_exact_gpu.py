@@ -50,6 +50,17 @@ def test_exact_equals_oracle(cuda, qblock, splits, M, N, K):
 
 
 @pytest.mark.parametrize("qblock", [32, 16])
+def test_exact_large_split_runs_in_cta(cuda, qblock):
+    """A split problem too large for the parallel-slice partial buffer (8 x M x N
+    x 4 bytes > 64 MB): the slices run one after another inside each CTA."""
+    M, N, K = 1000, 2100, 512
+    ca, cb, sa, sb, A, As, B, Bs = _operands(M, N, K, qblock, 55 + qblock, cuda)
+    got = ops.gemm_int4(A, As, B, Bs, None, torch.float32, splits=3, qblock=qblock).cpu().numpy()
+    want = O.block_int_matmul(ca, sa, cb, sb, None, block=qblock, splits=3)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("qblock", [32, 16])
 def test_exact_no_bias_and_auto_splits(cuda, qblock):
     M, N, K = 5, 96, 2048
     ca, cb, sa, sb, A, As, B, Bs = _operands(M, N, K, qblock, 7 + qblock, cuda)
@@ -139,17 +150,19 @@ def test_exact_equals_reference_kernel(cuda, ref, out_dtype, qblock, M, N, K):
     assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
 
 
+@pytest.mark.parametrize("M", [4608, 16, 1])
 @pytest.mark.parametrize("name,K,N", [("qkv", 3072, 9216), ("mlp_down", 12288, 3072)])
-def test_exact_flux_full_size_equals_reference_kernel(cuda, ref, name, K, N):
-    """Full-size Flux shapes at M = 4608, every output element, bf16 output:
-    the quantize_int4 activations of a seeded N(0,1) x and RTN weights."""
-    M = 4608
-    g = torch.Generator().manual_seed(K + N)
+def test_exact_flux_full_size_equals_reference_kernel(cuda, ref, name, K, N, M):
+    """Full-size Flux shapes, every output element, bf16 output, the default
+    split plan (M = 4608: one slice; M = 16 / 1: the reference splits K 3-8 ways
+    and the slices run as parallel work items): the quantize_int4 activations
+    of a seeded N(0,1) x and RTN weights against the reference's kernel."""
+    g = torch.Generator().manual_seed(K + N + M)
     x = torch.randn(M, K, generator=g).to(cuda)
     w = (torch.randn(N, K, generator=g) * 0.02).to(cuda)
     A, As = ops.quantize_int4(x)
     B, Bs = ops.quantize_int4(w)
-    want = _ref_gemm(ref, A, As, B, Bs, None, torch.bfloat16, 32, 1)
+    splits = ops.gemm_int4_auto_splits(M, N, K)
+    want = _ref_gemm(ref, A, As, B, Bs, None, torch.bfloat16, 32, splits)
     got = ops.gemm_int4(A, As, B, Bs, None, torch.bfloat16)
-    assert ops.gemm_int4_auto_splits(M, N, K) == 1
     assert torch.equal(got, want)
