@@ -59,9 +59,6 @@ constexpr int kProducerWarp = 0, kMmaWarp = 1, kUnpackWarp0 = 2, kUnpackWarps = 
               kRescaleWarps = 16;
 constexpr int kThreads = (kRescaleWarp0 + kRescaleWarps) * 32;
 constexpr int kSmemLimit = 232448;
-#ifndef GFX_W4A4X_BATCH_MMA
-#define GFX_W4A4X_BATCH_MMA 0
-#endif
 
 // Token tile per template: 128 tokens for 32-element blocks, 64 when the
 // rescale threads also carry the split partial sum or (qblock 16) two
@@ -408,25 +405,6 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
         const uint32_t xa = smem_u32(sm.stage0 + s * kStageBytes);
         const uint64_t adesc = tc::sw128_desc(xa + kActBytes), bdesc = tc::sw128_desc(xa);
         const int nblk = kb1 - ks * kBlocks < kBlocks ? kb1 - ks * kBlocks : kBlocks;
-#if GFX_W4A4X_BATCH_MMA
-        // every slot of the stage free first, then the stage's MMAs back to back
-        for (int j = 0; j < nblk && ok; ++j) {
-          const uint32_t b = bit + j;
-          if (!mbar_wait(&sm.dempty[b % kSlots], ((b / kSlots) & 1) ^ 1, kDevErrMmaBarrierTimeout)) ok = false;
-        }
-        if (!ok) break;
-        tc::tc_fence_after();
-        if (lane == 0) {
-          for (int j = 0; j < nblk; ++j) {
-            const int slot = (bit + j) % kSlots;
-            tc::umma_f8f6f4(tmem + slot * kCols, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), kId, 0u);
-            tc::umma_commit<1>(&sm.dfull[slot]);
-          }
-          tc::umma_commit<1>(&sm.empty[s]);
-        }
-        __syncwarp();
-        bit += nblk;
-#else
         for (int j = 0; j < nblk; ++j, ++bit) {
           const int slot = bit % kSlots;
           if (!mbar_wait(&sm.dempty[slot], ((bit / kSlots) & 1) ^ 1, kDevErrMmaBarrierTimeout)) {
@@ -443,7 +421,6 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4x_kernel(const __grid_constan
           }
           __syncwarp();
         }
-#endif
       }
     }
     if (lane == 0) tc::umma_commit<1>(sm.drain);
