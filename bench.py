@@ -62,7 +62,8 @@ def workload_config(world: int) -> dict:
             "weights": "int4 group-32, ggml Q4_0 synthetic (fp16-exact scales)",
             "l2": "each step reads > 126 MB of distinct inputs (no flush needed)",
             "parallelism": ("single GPU" if world == 1 else
-                            f"token rows / {world} (weights replicated), all_gather_into_tensor of y timed")}
+                            f"token rows / {world} (weights replicated), y all-gathered to every rank inside the "
+                            "timed region")}
 
 
 class ClockSampler:
@@ -327,6 +328,12 @@ def run_ours(args, world, rank, local):
     if world > 1:
         import torch.distributed as dist
     yfull = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for (_, _, N, _, _) in weights] if world > 1 else None
+    # N > 1: each GEMM's epilogue stores its rows into every rank's y (symmetric memory over NVLink), then a
+    # flag barrier; --nccl-gather uses a separate all_gather_into_tensor per GEMM instead
+    gather = None
+    if world > 1 and not args.nccl_gather:
+        from comfy_ui_gfx906_tools_b200.parallel import SymmetricRowGather
+        gather = SymmetricRowGather(M, max(N for (_, _, N, _, _) in weights), torch.bfloat16, dev)
 
     # --- device-resident timed loop ---
     # per-launch CUDA events inside the timed region itself (same clocks and
@@ -343,10 +350,13 @@ def run_ours(args, world, rank, local):
         for i, ((_, K, N, p, s), x) in enumerate(zip(weights, xloc)):
             if k >= 0:
                 ev[k][i][0].record(stream)
-            y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+            if gather is not None:  # GEMM + all-gather in one kernel, then the flag barrier
+                gather.gemm(x, p, s, None, r0, M)
+            else:
+                y = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
             if k >= 0:
                 ev[k][i][1].record(stream)
-            if world > 1:  # this GEMM's rows to every rank, overlapped with the next GEMM
+            if world > 1 and gather is None:  # this GEMM's rows to every rank, overlapped with the next GEMM
                 works.append(dist.all_gather_into_tensor(yfull[i], y, async_op=True))
         for w in works:
             w.wait()
@@ -371,7 +381,10 @@ def run_ours(args, world, rank, local):
     parity = {}
     rows = torch.randperm(M, generator=torch.Generator().manual_seed(5))[:64].sort().values.to(dev)
     for i, ((name, K, N, p, s), x) in enumerate(zip(weights, xs)):
-        y = yfull[i] if world > 1 else ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
+        if gather is not None:
+            y = gather.gemm(xloc[i], p, s, None, r0, M).clone()
+        else:
+            y = yfull[i] if world > 1 else ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
         ent = parity_of(y[rows].float(), torch_reference_rows(x, p, s, rows))
         if world > 1:
             whole = ops.gemm_w4a16(x, p, s, None, torch.bfloat16)
@@ -516,7 +529,9 @@ def run_ours(args, world, rank, local):
                          "peak_kind": f"bf16 dense burst ({pk['source']}): the 20-step timed loop is ~45 ms",
                          "frac_of_sustained": achieved / pk["bf16_tflops_sustained"],
                          "step_frac": (value / world) / peak, "traffic": traffic,
-                         "kernel": "wq_tc_kernel<1, bf16, 1> (tcgen05), mean over the six shapes' launches",
+                         "kernel": ("wq_tc_kernel<1, bf16, 1> (tcgen05), mean over the six shapes' launches" +
+                                    ("; with the fused all-gather, each launch's time includes its peer stores "
+                                     "and the flag barrier" if gather is not None else "")),
                          "launch_ms": {weights[i][0]: launch_ms[i] / args.steps for i in range(len(weights))}},
             "parity": {"ok": parity_ok, "rows_sampled": 64, "per_shape": parity,
                        "reference": "torch fp32 dequant-then-matmul of the sampled rows (north-star tolerance "
@@ -524,6 +539,9 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8, "w4a4_exact": w4a4,
             **({"small_m_channel_split": tp} if tp is not None else {}),
             **({"dit_rows": dit} if dit is not None else {}),
+            **({"allgather": ("fused: each GEMM's epilogue stores its rows into every rank's y (symmetric memory, "
+                              "NVLink peer stores), then a flag barrier kernel" if gather is not None else
+                              "NCCL all_gather_into_tensor per GEMM, async on NCCL's stream")} if world > 1 else {}),
             "gpu_launches": args.steps * len(weights), "clocks": clocks.summary(),
         }
         print(json.dumps(out))
@@ -736,6 +754,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-int8", action="store_true")
     ap.add_argument("--no-dit", action="store_true")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="N > 1: all-gather y with NCCL after each GEMM instead of the GEMM's own peer stores")
     ap.add_argument("--workload", choices=["gemm", "dit"], default="gemm")
     ap.add_argument("--res", type=int, default=1024, help="dit: latent resolution in pixels (1024 or 2048)")
     ap.add_argument("--split", choices=["batch", "rows"], default="batch", help="dit: how N > 1 ranks split")

@@ -38,6 +38,9 @@ SIGNATURES = {
     "w4a16_gemm_allgather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,
                                       _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_size_t,
                                       _c_void_p]),
+    "w4a16_gemm_rows_allgather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,
+                                           _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,
+                                           _c_size_t, _c_void_p]),
     "gfx_peer_barrier": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p]),
     "repack_q8_0": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "hadamard_rotate": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int64, _c_int, _c_int, _c_void_p]),

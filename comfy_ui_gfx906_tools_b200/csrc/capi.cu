@@ -408,6 +408,39 @@ int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const voi
                                      sm_count(current_device()));
 }
 
+int w4a16_gemm_rows_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+                              const void* bias, void* const* y_ranks, int n_ranks, int row0, int out_dtype, int M,
+                              int N, int K, int splits, void* workspace, size_t workspace_bytes, gfx_stream_t stream) {
+  const char* fn = "w4a16_gemm_rows_allgather";
+  if (n_ranks < 1 || n_ranks > gfx::kMaxOutTargets || row0 < 0 || !y_ranks)
+    return set_error(GFX_ERR_INVALID, "%s: need 1 <= n_ranks <= %d, row0 >= 0 and the ranks' output pointers "
+                     "(got n_ranks=%d row0=%d)", fn, gfx::kMaxOutTargets, n_ranks, row0);
+  for (int q = 0; q < n_ranks; ++q)
+    if (!y_ranks[q]) return set_error(GFX_ERR_INVALID, "%s: output pointer of rank %d is null", fn, q);
+  int rc = check_gemm_common(fn, x, x_dtype, w_q4, w_scale, scale_dtype, y_ranks[0], out_dtype, M, N, K, splits);
+  if (rc) return rc;
+  if (M == 0) return GFX_OK;
+  const int dev = current_device();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = check_device_health(fn, dev, workspace, workspace_bytes >= kSplitKCounterBytes ? kSplitKCounterBytes : 0, st);
+  if (rc) return rc;
+  const size_t elem = out_dtype == GFX_DTYPE_F32 ? 4 : 2;
+  gfx::OutTargets t{};
+  for (int q = 0; q < n_ranks; ++q) t.ptr[q] = static_cast<char*>(y_ranks[q]) + (size_t)row0 * N * elem;
+  t.count = n_ranks;
+  t.ldy = N;
+  t.col0 = 0;
+  t.fence_sys = 1;
+  if (M > 64) {
+    if (!w4a16_tc_supported(M, N, K, scale_dtype))
+      return set_error(GFX_ERR_UNSUPPORTED, "%s: K=%d with scale dtype %d is not supported for M > 64", fn, K,
+                       scale_dtype);
+    return launch_w4a16_tc_targets(x, w_q4, w_scale, scale_dtype, bias, t, out_dtype, M, N, K, st, sm_count(dev));
+  }
+  return launch_w4a16_smallm_targets(x, w_q4, w_scale, scale_dtype, bias, t, out_dtype, M, N, K, splits, workspace,
+                                     workspace_bytes, st, sm_count(dev));
+}
+
 int gfx_peer_barrier(int* const* flags_ranks, int n_ranks, int rank, gfx_stream_t stream) {
   if (n_ranks < 1 || n_ranks > gfx::kMaxOutTargets || rank < 0 || rank >= n_ranks || !flags_ranks)
     return set_error(GFX_ERR_INVALID, "gfx_peer_barrier: need 1 <= n_ranks <= %d and 0 <= rank < n_ranks",

@@ -48,6 +48,10 @@ int smallm_device_status(int clear);
 // qblock 32 (fp32 or fp16 scales [N, K/32]) or 16 (fp32 scales [N, K/16]; any M)
 int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias, void* y,
                     int out_dtype, int M, int N, int K, cudaStream_t stream, int sms, int qblock = 32);
+// The same GEMM storing y into tg.count buffers (tg.ptr[q][m * tg.ldy + n], fp32 or fp16 32-groups, one CTA
+// per tile) and fencing at system scope: the token-row split's GEMM and all-gather in one kernel.
+int launch_w4a16_tc_targets(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias,
+                            const OutTargets& tg, int out_dtype, int M, int N, int K, cudaStream_t stream, int sms);
 bool w4a16_tc_supported(int M, int N, int K, int scale_dtype);
 int tc_device_status(int clear);
 int selftest_device_status(int clear);

@@ -210,13 +210,18 @@ struct Smem {
   uint32_t* tmem_base;
 };
 
-template <int F, typename OutT, int C>
+// kPeers: the epilogue stores every output element into each of tg.count
+// buffers (tg.ptr[q][m * tg.ldy + n], e.g. every rank's y mapped over NVLink,
+// offset to this rank's rows), then fences at system scope: the GEMM and the
+// all-gather of a token-row split in one kernel.
+template <int F, typename OutT, int C, bool kPeers = false>
 __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constant__ CUtensorMap x_map,
                                                             const __grid_constant__ CUtensorMap q_map,
                                                             const __grid_constant__ CUtensorMap s_map, int scale_tma,
                                                             const void* __restrict__ wscale,
                                                             const OutT* __restrict__ bias, OutT* __restrict__ y,
-                                                            int M, int N, int K, int* status_host) {
+                                                            int M, int N, int K, int* status_host,
+                                                            const __grid_constant__ OutTargets tg) {
   using T = Traits<F, C>;
   constexpr int kStages = T::kStages;
   constexpr int kStageBytes = T::kStageBytes;
@@ -557,7 +562,14 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
           for (int j = 0; j < 32; ++j) {
             const int m = mbase + j;
             const float a = T::kChannel ? __fmul_rn(__uint_as_float(v[j]), cs) : __uint_as_float(v[j]);
-            if (m < M) y[(size_t)m * N + n] = from_f32<OutT>(a + b);
+            if (m < M) {
+              const OutT v = from_f32<OutT>(a + b);
+              if constexpr (kPeers) {
+                for (int t = 0; t < tg.count; ++t) static_cast<OutT*>(tg.ptr[t])[(size_t)m * tg.ldy + n] = v;
+              } else {
+                y[(size_t)m * N + n] = v;
+              }
+            }
           }
         }
       }
@@ -573,6 +585,9 @@ __global__ void __launch_bounds__(kThreads, 1) wq_tc_kernel(const __grid_constan
     }
   }
 
+  if constexpr (kPeers) {
+    if (warp < kEpiWarps) __threadfence_system();  // the peer stores are visible before the flag barrier
+  }
   if (!ok) mirror_device_error(status_host);
   tc_fence_before();
   if constexpr (C == 2) {
@@ -608,11 +623,12 @@ static int tc_ctas(int M) {
   return 1;
 }
 
-template <int F, typename OutT, int C>
+template <int F, typename OutT, int C, bool kPeers = false>
 static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const CUtensorMap& sm_map, int scale_tma,
-                       const void* ws, const void* bias, void* y, int M, int N, int K, cudaStream_t st, int sms) {
+                       const void* ws, const void* bias, void* y, int M, int N, int K, cudaStream_t st, int sms,
+                       const OutTargets* tg = nullptr) {
   using T = tc::Traits<F, C>;
-  auto kern = tc::wq_tc_kernel<F, OutT, C>;
+  auto kern = tc::wq_tc_kernel<F, OutT, C, kPeers>;
   static bool attr_set[64] = {false};
   static int max_clusters[64] = {0};
   const int dev = current_device();
@@ -659,16 +675,17 @@ static int launch_tc_t(const CUtensorMap& xm, const CUtensorMap& qm, const CUten
   const int tiles = ((N + rows - 1) / rows) * ((M + tc::kTileM - 1) / tc::kTileM);
   const int units = tiles < clusters ? tiles : clusters;
   cfg.gridDim = dim3(C * units);
+  OutTargets none{};
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xm, qm, sm_map, scale_tma, ws, (const OutT*)bias, (OutT*)y, M, N, K,
-                                     host_status_word(dev));
+                                     host_status_word(dev), tg ? *tg : none);
   if (e != cudaSuccess) return set_error(GFX_ERR_CUDA, "wq_tc_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("wq_tc_kernel");
 }
 
 template <int F>
 static int launch_tc_out(int out_dtype, const void* x, const CUtensorMap& qm, const void* ws, const void* bias,
-                         void* y, int M, int N, int K, cudaStream_t st, int sms) {
-  const int C = tc_ctas(M);
+                         void* y, int M, int N, int K, cudaStream_t st, int sms, const OutTargets* tg = nullptr) {
+  const int C = tg ? 1 : tc_ctas(M);
   CUtensorMap xm;
   // x box: 64 K-elements x (256 tokens, or the 128 of one CTA of a pair), SWIZZLE_128B
   int rc = make_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
@@ -691,6 +708,17 @@ static int launch_tc_out(int out_dtype, const void* x, const CUtensorMap& qm, co
                           CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;
       scale_tma = 1;
+    }
+  }
+  if (tg != nullptr) {
+    if constexpr (F == tc::kInt4GroupF32 || F == tc::kInt4GroupF16) {
+      if (out_dtype == GFX_DTYPE_F32)
+        return launch_tc_t<F, float, 1, true>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms, tg);
+      if (out_dtype == GFX_DTYPE_F16)
+        return launch_tc_t<F, __half, 1, true>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms, tg);
+      return launch_tc_t<F, __nv_bfloat16, 1, true>(xm, qm, sm_map, scale_tma, ws, bias, y, M, N, K, st, sms, tg);
+    } else {
+      return set_error(GFX_ERR_UNSUPPORTED, "wq_tc: peer-store outputs take int4 weights with 32-element groups");
     }
   }
   if (C == 2) {
@@ -717,6 +745,17 @@ int launch_w4a16_tc(const void* x, const void* wq, const void* ws, int scale_dty
   if (scale_dtype == GFX_SCALE_F16)
     return launch_tc_out<tc::kInt4GroupF16>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
   return launch_tc_out<tc::kInt4GroupF32>(out_dtype, x, qm, ws, bias, y, M, N, K, stream, sms);
+}
+
+int launch_w4a16_tc_targets(const void* x, const void* wq, const void* ws, int scale_dtype, const void* bias,
+                            const OutTargets& tg, int out_dtype, int M, int N, int K, cudaStream_t stream, int sms) {
+  CUtensorMap qm;
+  int rc = cached_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                          tc::kStageK / 2, tc::kTileN, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  if (scale_dtype == GFX_SCALE_F16)
+    return launch_tc_out<tc::kInt4GroupF16>(out_dtype, x, qm, ws, bias, tg.ptr[0], M, N, K, stream, sms, &tg);
+  return launch_tc_out<tc::kInt4GroupF32>(out_dtype, x, qm, ws, bias, tg.ptr[0], M, N, K, stream, sms, &tg);
 }
 
 int launch_w8a16_tc(const void* x, const void* wq, const void* ws, int per_channel, const void* bias, void* y,

@@ -210,6 +210,75 @@ class SymmetricAllGather:
         return self.ybuf[parity, :M * n_total].view(M, n_total)
 
 
+class SymmetricRowGather:
+    """The token-row split of a linear with its all-gather fused into the GEMM
+    (``w4a16_gemm_rows_allgather`` then ``gfx_peer_barrier``).
+
+    y buffers [m_max, n_max] live in symmetric memory (every rank maps every
+    rank's buffers over NVLink). Rank r computes its rows [row0, row0 + M) and
+    the GEMM's epilogue stores them into the same rows of EVERY rank's y, tile
+    by tile as they are computed, so the transfer overlaps the math and no
+    collective kernel competes for SMs; the flag barrier then makes the whole
+    y visible. Two buffers alternate between calls (as in SymmetricAllGather:
+    a buffer is rewritten only after the barrier of the call in between).
+    ``strict`` synchronises after every barrier and raises on a peer timeout.
+    """
+
+    def __init__(self, m_max: int, n_max: int, dtype: torch.dtype, device: torch.device, group=None,
+                 strict: bool = False):
+        import ctypes
+        import torch.distributed._symmetric_memory as symm_mem
+        self.strict = strict
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.m_max, self.n_max, self.dtype, self.device = m_max, n_max, dtype, device
+        group_name = (group or dist.group.WORLD).group_name
+        self.ybuf = symm_mem.empty((2, m_max * n_max), dtype=dtype, device=device)
+        y_ptrs = list(symm_mem.rendezvous(self.ybuf, group_name).buffer_ptrs)
+        self.flags = symm_mem.empty((self.world + 1,), dtype=torch.int32, device=device)
+        self.flags.zero_()
+        f_ptrs = list(symm_mem.rendezvous(self.flags, group_name).buffer_ptrs)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before the first barrier
+        row = m_max * n_max * self.ybuf.element_size()
+        self._target_arrs = [(ctypes.c_void_p * self.world)(*[p + k * row for p in y_ptrs]) for k in (0, 1)]
+        self._targets = [ctypes.cast(a, ctypes.c_void_p) for a in self._target_arrs]
+        self._flag_arr = (ctypes.c_void_p * self.world)(*f_ptrs)
+        self._flag_ptr = ctypes.cast(self._flag_arr, ctypes.c_void_p)
+        self.calls = 0
+
+    def gemm(self, x_local: torch.Tensor, w_q4: torch.Tensor, scale: torch.Tensor, bias, row0: int,
+             m_total: int) -> torch.Tensor:
+        """y[m_total, N] (a view of the current buffer, valid until two calls
+        later): every rank's rows of x @ dequant(w)^T (+ bias), this rank's
+        x_local (bf16 [M, K] contiguous) being rows [row0, row0 + M)."""
+        from . import _lib, ops
+        M, K = x_local.shape
+        N = w_q4.shape[0]
+        if m_total > self.m_max or N > self.n_max or row0 + M > m_total:
+            raise ValueError(f"row gather takes m_total <= {self.m_max}, N <= {self.n_max}, row0 + M <= m_total; "
+                             f"got m_total={m_total}, N={N}, row0={row0}, M={M}")
+        parity = self.calls & 1
+        self.calls += 1
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            L = _lib.load()
+            ws = ops._workspace(self.device, stream, int(L.w4a16_workspace_bytes(M, N, K, 0))) if M <= 64 else None
+            ops._call_gemm("w4a16_gemm_rows_allgather", self.device, x_local.data_ptr(), _lib.DTYPE_BF16,
+                           w_q4.data_ptr(), scale.data_ptr(),
+                           _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32,
+                           bias.data_ptr() if bias is not None else None, self._targets[parity], self.world, row0,
+                           ops._dtype_code(self.dtype), M, N, K, 0, ws.data_ptr() if ws is not None else None,
+                           ws.numel() if ws is not None else 0, stream)
+            _lib.call("gfx_peer_barrier", self._flag_ptr, self.world, self.rank, stream)
+            status = ops.device_status(self.device) if self.strict else 0
+            if status != 0:
+                raise _lib.GfxError("gfx_peer_barrier", _lib.GFX_ERR_DEVICE,
+                                    f"device status {status} after the fused row all-gather (a peer did not reach "
+                                    "the barrier within its 2 s budget)")
+        return self.ybuf[parity, :m_total * N].view(m_total, N)
+
+
 class ChannelShardLinear(torch.nn.Module):
     """Output-channel split of one int4 linear for the M <= 16 (HBM-bound) case.
 

@@ -74,6 +74,21 @@ int w4a16_gemm_allgather(const void* x, int x_dtype, const void* w_q4, const voi
                          int N_local, int K, int splits, void* workspace, size_t workspace_bytes,
                          gfx_stream_t stream);
 
+/* Token-row split of one W4A16 GEMM with the all-gather fused into its
+ * epilogue (no reference counterpart: the reference splits a DiT's image rows
+ * across two GPUs and exchanges K/V, row_split.py:122-241; this is the B200
+ * form of the token-row split of one linear, the survey's first multi-GPU
+ * case). This rank computes rows [row0, row0 + M) of y from its activations
+ * x [M, K] and stores them into EVERY rank's y buffer (y_ranks[q]: rank q's
+ * [M_total, N] buffer, mapped on this device, e.g. symmetric memory reached
+ * over NVLink) with plain stores and a system-scope fence; M > 64 runs the
+ * tcgen05 kernel (fp32 or fp16 32-group scales), M <= 64 the small-M kernel.
+ * Follow it with gfx_peer_barrier before reading y. Other arguments as
+ * w4a16_gemm. */
+int w4a16_gemm_rows_allgather(const void* x, int x_dtype, const void* w_q4, const void* w_scale, int scale_dtype,
+                              const void* bias, void* const* y_ranks, int n_ranks, int row0, int out_dtype, int M,
+                              int N, int K, int splits, void* workspace, size_t workspace_bytes, gfx_stream_t stream);
+
 /* Cross-GPU barrier over NVLink-mapped flags (no reference counterpart):
  * flags_ranks[q] is rank q's int[n_ranks + 1] (zero before the first call).
  * The epoch lives on the device: slot n_ranks of this rank's own array counts

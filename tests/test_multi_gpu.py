@@ -1,6 +1,7 @@
 """Splits across two GPUs over NCCL (skipped with fewer than two GPUs): the
 output-channel split (NCCL all-gather, and the fused kernel that stores into every rank's
-symmetric-memory buffer), the token-row split of an int4 linear and the batch / token-row splits of an
+symmetric-memory buffer), the token-row split of an int4 linear (torch all-gather, and the GEMM whose
+epilogue stores its rows into every rank's buffer) and the batch / token-row splits of an
 int4 DiT match the same computation on one GPU. Every rank runs as its own
 spawned process with a short process-group timeout."""
 import datetime
@@ -81,6 +82,24 @@ def _worker(rank, world, port, q):
         ref = lin(xt).float()
         got = parallel.token_shard_linear(lin, xt).float()
         out["tokens"] = float((got - ref).abs().max() / ref.abs().max())
+        # token-row split with the all-gather fused into the GEMM: each rank's epilogue stores its rows into
+        # every rank's symmetric-memory y; M = 600 (tcgen05 kernel, 300 rows per rank) and M = 40 (small-M
+        # kernel); several calls so both buffers are reused. Each rank's rows must equal the plain kernel
+        # run on the same rows (same M, same plan), bit for bit.
+        rg = parallel.SymmetricRowGather(600, N, torch.bfloat16, dev)
+        bad = []
+        for call, mt in enumerate((600, 40, 600, 40)):
+            xa = synthetic.activations(mt, K, seed=30 + mt).to(dev)
+            per = mt // world
+            yg = rg.gemm(xa[rank * per:(rank + 1) * per].contiguous(), p, s, None, rank * per, mt).clone()
+            torch.cuda.synchronize()
+            for q in range(world):
+                want = ops.gemm_w4a16(xa[q * per:(q + 1) * per].contiguous(), p, s, None, torch.bfloat16)
+                got = yg[q * per:(q + 1) * per]
+                if not torch.equal(got, want):
+                    bad.append((call, mt, q, float((got.float() - want.float()).abs().max())))
+        out["rowgather_bad"] = bad
+        out["rowgather_status"] = int(_lib.load().gfx_device_status(1))
         # int4 DiT (tiny): batch split and token-row split against the one-GPU forward
         cfg = flux_dit.tiny_config(depth_double=2, depth_single=2)
         model = flux_dit.FluxDiT(cfg, flux_dit.int4_linear_factory(dev, seed=11), dev)
@@ -118,5 +137,7 @@ def test_two_gpu_splits_match_one_gpu():
         assert val["fused_exact"] and val["fused_status"] == 0 and val["fused_vs_one"] < 1e-2, val
         assert val["fused_graph_exact"] and val["fused_graph_status"] == 0, val
         assert val["tokens"] < 1e-6, val  # the same rows through the same kernel
+        assert not val["rowgather_bad"] and val["rowgather_status"] == 0, (val["rowgather_bad"],
+                                                                            val["rowgather_status"])
         # bf16 activations through 4 blocks; the split changes only which GPU computes what
         assert val["batch"] < 2e-2 and val["rows"] < 2e-2, val
