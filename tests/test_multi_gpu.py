@@ -93,11 +93,11 @@ def _worker(rank, world, port, q):
             per = mt // world
             yg = rg.gemm(xa[rank * per:(rank + 1) * per].contiguous(), p, s, None, rank * per, mt).clone()
             torch.cuda.synchronize()
-            for q in range(world):
-                want = ops.gemm_w4a16(xa[q * per:(q + 1) * per].contiguous(), p, s, None, torch.bfloat16)
-                got = yg[q * per:(q + 1) * per]
+            for src in range(world):
+                want = ops.gemm_w4a16(xa[src * per:(src + 1) * per].contiguous(), p, s, None, torch.bfloat16)
+                got = yg[src * per:(src + 1) * per]
                 if not torch.equal(got, want):
-                    bad.append((call, mt, q, float((got.float() - want.float()).abs().max())))
+                    bad.append((call, mt, src, float((got.float() - want.float()).abs().max())))
         out["rowgather_bad"] = bad
         out["rowgather_status"] = int(_lib.load().gfx_device_status(1))
         # int4 DiT (tiny): batch split and token-row split against the one-GPU forward
