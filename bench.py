@@ -530,7 +530,7 @@ def run_ours(args, world, rank, local):
                          "peak_kind": f"bf16 dense burst ({pk['source']}): the 20-step timed loop is ~45 ms",
                          "frac_of_sustained": achieved / pk["bf16_tflops_sustained"],
                          "step_frac": (value / world) / peak, "traffic": traffic,
-                         "kernel": ("wq_tc_kernel<1, bf16, 1> (tcgen05), mean over the six shapes' launches" +
+                         "kernel": ("wq_tc_kernel<1, bf16, 1, false> (tcgen05), mean over the six shapes' launches" +
                                     ("; with the fused all-gather, each launch's time includes its peer stores "
                                      "and the flag barrier" if gather is not None else "")),
                          "launch_ms": {weights[i][0]: launch_ms[i] / args.steps for i in range(len(weights))}},
