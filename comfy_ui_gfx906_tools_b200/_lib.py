@@ -66,6 +66,10 @@ SIGNATURES = {
                                     _c_void_p, _c_void_p]),
     "quantize_int4_cols": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int, ctypes.c_uint32,
                                     _c_void_p, _c_void_p, _c_void_p]),
+    "attention": (_c_int, [_c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                           _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, ctypes.c_float, _c_void_p]),
+    "attention_block_rows": (_c_int, [_c_int]),
+    "attention_max_tiles": (_c_int, []),
     "w4a4_gemm_exact_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "w4a4_gemm_exact_splits": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
     "w4a4_gemm_exact": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,

@@ -349,6 +349,47 @@ int w4a4_gemm_exact(const void* a_q4, const float* a_scale, const void* b_q4, co
                            sm_count(dev));
 }
 
+int attention_block_rows(int qk_mode) {
+  if (qk_mode < 0 || qk_mode > 2) {
+    set_error(GFX_ERR_INVALID, "attention_block_rows: qk_mode must be 0 fp16 / 1 int8 / 2 int4, got %d", qk_mode);
+    return -1;
+  }
+  return attention_rows_per_block(qk_mode);
+}
+
+int attention_max_tiles(void) { return kAttentionMaxTiles; }
+
+int attention(int qk_mode, int pv_mode, const void* q, const float* q_scale, const void* k, const float* k_scale,
+              const void* vt, const float* v_scale, const uint8_t* keep, void* out, int B, int H, int KVH, int Lq,
+              int Lk, float skip_below, gfx_stream_t stream) {
+  const char* fn = "attention";
+  if (qk_mode < 0 || qk_mode > 2)
+    return set_error(GFX_ERR_INVALID, "%s: qk_mode must be 0 fp16 / 1 int8 / 2 int4, got %d", fn, qk_mode);
+  if (pv_mode < 0 || pv_mode > 1)
+    return set_error(GFX_ERR_INVALID, "%s: pv_mode must be 0 fp16 / 1 u8, got %d", fn, pv_mode);
+  if (B < 0 || H < 0 || Lq < 0 || KVH <= 0 || Lk <= 0 || H % KVH != 0)
+    return set_error(GFX_ERR_INVALID, "%s: need B, H, Lq >= 0, Lk >= 1 and H (%d) a multiple of KVH (%d); got B=%d "
+                     "Lq=%d Lk=%d", fn, H, KVH, B, Lq, Lk);
+  if (!q || !k || !vt || !out)
+    return set_error(GFX_ERR_INVALID, "%s: Q, K, Vt and out must be device pointers", fn);
+  if (qk_mode != 0 && (!q_scale || !k_scale))
+    return set_error(GFX_ERR_INVALID, "%s: the int Q.K modes need q_scale and k_scale", fn);
+  if (pv_mode == 1 && !v_scale) return set_error(GFX_ERR_INVALID, "%s: the u8 P.V mode needs v_scale", fn);
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k) & 15) ||
+      (reinterpret_cast<uintptr_t>(vt) & 15) || (reinterpret_cast<uintptr_t>(out) & 3) ||
+      (reinterpret_cast<uintptr_t>(q_scale) & 3) || (reinterpret_cast<uintptr_t>(k_scale) & 3) ||
+      (reinterpret_cast<uintptr_t>(v_scale) & 3))
+    return set_error(GFX_ERR_INVALID, "%s: Q, K and Vt must be 16-byte aligned, out and the scales 4-byte aligned", fn);
+  const long long n_tiles = (Lk + 63) / 64;
+  if (keep && n_tiles > kAttentionMaxTiles)
+    return set_error(GFX_ERR_INVALID, "%s: keep supports at most %d key tiles, got %lld", fn, kAttentionMaxTiles,
+                     n_tiles);
+  if (H > 65535 || B > 65535)
+    return set_error(GFX_ERR_UNSUPPORTED, "%s: at most 65535 heads and batches, got H=%d B=%d", fn, H, B);
+  return launch_attention(qk_mode, pv_mode, q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk,
+                          skip_below, reinterpret_cast<cudaStream_t>(stream));
+}
+
 static int check_train_quant(const char* fn, const void* x, int64_t row_stride, int R, int C, int mult_r, int mult_c,
                              const void* packed, const void* scale) {
   if (!x || !packed || !scale) return set_error(GFX_ERR_INVALID, "%s: x, packed and scale must be device pointers", fn);

@@ -76,6 +76,14 @@ int launch_quantize_int4_rows(const void* x, long long row_stride, int R, int C,
 int launch_quantize_int4_cols(const void* x, long long row_stride, int R, int C, const float* signs, int sr,
                               uint32_t seed, void* packed, float* scale, cudaStream_t stream);
 
+// fused quantized attention, head dim 128 -- attention.cu
+// qk_mode 0 fp16 / 1 int8 / 2 int4, pv_mode 0 fp16 / 1 u8; layouts as the C ABI's attention().
+constexpr int kAttentionMaxTiles = 1024;  // key tiles a keep mask may cover (65536 keys)
+int attention_rows_per_block(int qk_mode);
+int launch_attention(int qk_mode, int pv_mode, const void* q, const float* q_scale, const void* k,
+                     const float* k_scale, const void* vt, const float* v_scale, const uint8_t* keep, void* out,
+                     int B, int H, int KVH, int Lq, int Lk, float skip_below, cudaStream_t stream);
+
 // loaders / helpers -- pack.cu
 int launch_int4_dequant(const void* wq, const void* ws, int scale_dtype, void* out, int out_dtype, int N, int K,
                         cudaStream_t stream, int qblock = 32);

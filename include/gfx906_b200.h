@@ -186,6 +186,36 @@ int quantize_int4_cols(const void* x, int64_t row_stride, int R, int C, const fl
                        void* packed, float* scale, gfx_stream_t stream);
 
 /*
+ * Fused quantized attention, head dim 128 (attention(), binding.cpp:114-170;
+ * attention_kernel, attention.hip:83-357). Inputs as the reference's prepare
+ * step writes them (attention.py:50-81): scores in log2 units (softmax scale
+ * * log2(e) folded into Q, or into q_scale for the int modes).
+ *   qk_mode 0 fp16: Q [B, H, Lq, 128] / K [B, KVH, Lk, 128] fp16, no scales.
+ *   qk_mode 1 int8: Q, K int8 per token, q_scale [B, H, Lq], k_scale [B, KVH, Lk].
+ *   qk_mode 2 int4: Q, K packed int4 [.., 64 bytes] (element 2i in the low
+ *                   nibble of byte i), scales as int8.
+ *   pv_mode 0 fp16: Vt [B, KVH, ceil(Lk/64), 128, 64] fp16 (64-key tiles,
+ *                   channel-major), no v_scale.
+ *   pv_mode 1 u8:   Vt as above in uint8 (value + 128), v_scale
+ *                   [B, KVH, ceil(Lk/64), 128] fp32.
+ * keep: NULL or uint8 [B, H, ceil(Lq / attention_block_rows(qk_mode)),
+ * ceil(Lk/64)], nonzero = visit that key tile (at most attention_max_tiles()
+ * tiles; every query block must keep one). skip_below: a key tile whose
+ * largest attention weight is below this fraction of the running row maximum
+ * for all 16 rows of a warp skips its P.V (0 = never). H % KVH == 0 (GQA:
+ * head h reads KV head h / (H / KVH)). out: fp16 [B, Lq, H * 128].
+ * Q, K, Vt 16-byte aligned.
+ */
+int attention(int qk_mode, int pv_mode, const void* q, const float* q_scale, const void* k, const float* k_scale,
+              const void* vt, const float* v_scale, const uint8_t* keep, void* out, int B, int H, int KVH, int Lq,
+              int Lk, float skip_below, gfx_stream_t stream);
+/* Query rows per block of the keep mask (64 for fp16 Q.K, 128 for the int
+ * modes; attention_block_rows, binding.cpp:17), or -1 for a bad mode. */
+int attention_block_rows(int qk_mode);
+/* Key tiles a keep mask may cover (attention_max_tiles, binding.cpp:21). */
+int attention_max_tiles(void);
+
+/*
  * W4A16 GEMM that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a plugin host that passes
  * only its input/output device pointers and owns the memory budget, or code

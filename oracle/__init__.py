@@ -1,4 +1,4 @@
-"""CPU oracle for the int4/int8 weight-only linear path.
+"""CPU oracle for the int4/int8 weight-only linear path and the fused attention.
 
 TEST INFRASTRUCTURE ONLY. Nothing in the product package imports this
 package; only ``tests/``, ``__graft_entry__.smoke()`` and the
@@ -8,3 +8,4 @@ path. The GPU path fails loudly when its CUDA library is missing; it never
 falls back to anything here.
 """
 from .oracle import *  # noqa: F401,F403
+from .attention import *  # noqa: F401,F403
