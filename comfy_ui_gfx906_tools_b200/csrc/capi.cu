@@ -240,8 +240,8 @@ int gfx_device_status(int clear) {
   int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return -set_error(GFX_ERR_CUDA, "gfx_device_status: %s", cudaGetErrorString(e));
-  const int parts[4] = {smallm_device_status(clear), tc_device_status(clear), selftest_device_status(clear),
-                         w4a4x_device_status(clear)};
+  const int parts[5] = {smallm_device_status(clear), tc_device_status(clear), selftest_device_status(clear),
+                         w4a4x_device_status(clear), attn_tc_device_status(clear)};
   for (int p : parts) {
     if (p < 0) return -set_error(GFX_ERR_CUDA, "gfx_device_status: reading a status word failed");
     if (p && !v) v = p;
@@ -376,10 +376,10 @@ int attention(int qk_mode, int pv_mode, const void* q, const float* q_scale, con
     return set_error(GFX_ERR_INVALID, "%s: the int Q.K modes need q_scale and k_scale", fn);
   if (pv_mode == 1 && !v_scale) return set_error(GFX_ERR_INVALID, "%s: the u8 P.V mode needs v_scale", fn);
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k) & 15) ||
-      (reinterpret_cast<uintptr_t>(vt) & 15) || (reinterpret_cast<uintptr_t>(out) & 3) ||
+      (reinterpret_cast<uintptr_t>(vt) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
       (reinterpret_cast<uintptr_t>(q_scale) & 3) || (reinterpret_cast<uintptr_t>(k_scale) & 3) ||
       (reinterpret_cast<uintptr_t>(v_scale) & 3))
-    return set_error(GFX_ERR_INVALID, "%s: Q, K and Vt must be 16-byte aligned, out and the scales 4-byte aligned", fn);
+    return set_error(GFX_ERR_INVALID, "%s: Q, K, Vt and out must be 16-byte aligned, the scales 4-byte aligned", fn);
   const long long n_tiles = (Lk + 63) / 64;
   if (keep && n_tiles > kAttentionMaxTiles)
     return set_error(GFX_ERR_INVALID, "%s: keep supports at most %d key tiles, got %lld", fn, kAttentionMaxTiles,

@@ -56,6 +56,17 @@ def test_kernel_equals_oracle(cuda, qk, pv, B, H, KVH, Lq, Lk):
     _close(*_both(q, k, v, qk, pv))
 
 
+@pytest.mark.parametrize("qk,pv", [m for m in MODES if m[0] != "fp16"])
+@pytest.mark.parametrize("B,H,KVH,Lq,Lk", [(1, 8, 2, 300, 300), (2, 4, 4, 130, 333)])
+def test_mma_sync_kernel_equals_oracle(cuda, monkeypatch, qk, pv, B, H, KVH, Lq, Lk):
+    """The int Q.K modes run on the tcgen05 kernel (csrc/attention_tc.cu) by
+    default; GFX906_B200_ATTN_MMA_SYNC=1 selects the mma.sync kernel
+    (csrc/attention.cu), which must agree with the oracle as well."""
+    monkeypatch.setenv("GFX906_B200_ATTN_MMA_SYNC", "1")
+    q, k, v = _inputs(B, H, KVH, Lq, Lk, 31 + Lq + Lk + H, cuda)
+    _close(*_both(q, k, v, qk, pv))
+
+
 @pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "u8"), ("fp16", "fp16")])
 def test_kernel_keep_mask_equals_oracle(cuda, qk, pv):
     B, H, KVH, L = 1, 4, 2, 700
