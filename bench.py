@@ -468,6 +468,31 @@ def run_ours(args, world, rank, local):
                 "includes": "per call: e5m2 pre-pass of A, scale transpose, the GEMM"}
         del xq, w32
 
+    # --- the fused quantized attention (the reference's attention.hip; tests/test_attention_gpu.py):
+    # Flux 1024^2 attention, batch 1, 24 heads, 4096 image + 512 text tokens, head dim 128, on inputs
+    # prepared once (the kernel alone), with torch's SDPA on the same fp16 q / k / v for context ---
+    attn = None
+    if not args.no_attention and world == 1:
+        from comfy_ui_gfx906_tools_b200 import attention as fa
+        La, Ha = 4608, 24
+        ga = torch.Generator(device=dev).manual_seed(77)
+        qa, ka, va = (torch.randn(1, Ha, La, 128, device=dev, dtype=torch.float16, generator=ga) for _ in range(3))
+        flop_a = 4.0 * La * La * 128 * Ha
+        attn = {"unit": "TFLOP/s (4 * L^2 * 128 * heads)", "shape": {"batch": 1, "heads": Ha, "tokens": La},
+                "inputs": "prepared once, L2-resident (a compute-bound kernel)", "modes": {}}
+        for qk, pv in (("int4", "u8"), ("int8", "u8"), ("int8", "fp16"), ("fp16", "fp16")):
+            prep = (*fa.prepare_qk(qa, ka, qk), *fa.prepare_v(va, pv))
+            msa = time_steps(lambda: fa.attention_prepared(*prep, qk, pv, 1e-4), args.steps, args.warmup, world, dev,
+                             stream) / args.steps
+            attn["modes"][f"{qk}/{pv}"] = {"ms": msa, "value": flop_a / (msa * 1e-3) / 1e12,
+                                          "kernel": "attention_tc_kernel (tcgen05)" if qk != "fp16"
+                                          else "attention_kernel (mma.sync)"}
+            del prep
+        mss = time_steps(lambda: torch.nn.functional.scaled_dot_product_attention(qa, ka, va), args.steps,
+                         args.warmup, world, dev, stream) / args.steps
+        attn["torch_sdpa_fp16"] = {"ms": mss, "value": flop_a / (mss * 1e-3) / 1e12}
+        del qa, ka, va
+
     # --- e2e: public API with host buffers, H2D of x and D2H of y inside the timed region ---
     # (pinned host buffers; the copies of one step overlap its GEMMs and each other)
     e2e = None
@@ -538,6 +563,7 @@ def run_ours(args, world, rank, local):
                        "reference": "torch fp32 dequant-then-matmul of the sampled rows (north-star tolerance "
                                     "2e-2 max-abs ratio, 5e-3 mean relative error)"},
             "cpu_baseline": cpu, "e2e": e2e, "small_m": small, "int8": int8, "w4a4_exact": w4a4,
+            **({"attention": attn} if attn is not None else {}),
             **({"small_m_channel_split": tp} if tp is not None else {}),
             **({"dit_rows": dit} if dit is not None else {}),
             **({"allgather": ("fused: each GEMM's epilogue stores its rows into every rank's y (symmetric memory, "
@@ -755,6 +781,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-int8", action="store_true")
     ap.add_argument("--no-dit", action="store_true")
+    ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--fused-gather", action="store_true",
                     help="N > 1: all-gather y from the GEMM's own epilogue (peer stores + flag barrier) instead of "
                          "NCCL after each GEMM")

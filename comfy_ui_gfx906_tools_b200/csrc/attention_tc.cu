@@ -23,11 +23,17 @@
 //                  fp32 accumulators: u8 o = fma(rel/255 * v_scale,
 //                  (float)acc - 128 sum(pq), o) exactly as the reference;
 //                  fp16 o += O_t
-// K / V tiles and their scales are double-buffered (cp.async, the next
-// tile's copies in flight during this tile's work; int4 K goes through
-// registers and is sign-extended on the way into shared memory). Two CTAs per
-// SM (256 TMEM columns each) overlap one CTA's CUDA-core softmax / fold with
-// the other's MMAs. Every mbarrier wait is bounded (common.cuh); a CTA whose
+// Pipelining: S_{t+1} is issued together with O_t (S double-buffered in TMEM
+// columns [0, 64) / [64, 128)), so one block-wide barrier per tile suffices;
+// tile t+2's K / V / scales are copied (cp.async; int4 K through registers,
+// sign-extended on the way into shared memory) while tile t+1 is processed.
+// Two CTAs per SM (256 TMEM columns each) overlap one CTA's CUDA-core
+// softmax / fold with the other's MMAs. What bounds it (measured): the
+// per-row CUDA-core chain (scale, max, exp2, levels, fold: ~1000
+// instructions per row and tile) with two warps per SM sub-partition; the
+// MMAs are short. Measured alternatives that were slower: two threads per row
+// (halved chains, but an extra exchange barrier per tile and 128-register
+// spills). Every mbarrier wait is bounded (common.cuh); a CTA whose
 // wait gives up records the error, leaves its loop at the next block-wide
 // barrier, frees its TMEM and exits.
 #include <stdlib.h>
@@ -48,7 +54,7 @@ constexpr int kRows = 128;
 constexpr int kThreads = 128;
 constexpr float kNoScore = -1e30f;
 constexpr int kTmemCols = 256;
-constexpr int kTmemS = 0;     // S: 64 int32 columns
+constexpr int kTmemS = 0;     // S: two buffers of 64 int32 columns
 constexpr int kTmemO = 128;   // O_t: 128 columns
 
 template <int QK, int PV>
@@ -62,8 +68,8 @@ struct Cfg {
   static constexpr int kOffV = kOffK + 2 * kKBytes;  // 2 buffers
   static constexpr int kOffP = kOffV + 2 * kVBytes;
   static constexpr int kOffKs = kOffP + kPBytes;   // 2 x 64 floats
-  static constexpr int kOffVs = kOffKs + 2 * kTile * 4;  // 2 x 128 floats
-  static constexpr int kOffKeep = kOffVs + 2 * kD * 4;
+  static constexpr int kOffVs = kOffKs + 2 * kTile * 4;  // 3 x 128 floats (the fold reads them one tile behind)
+  static constexpr int kOffKeep = kOffVs + 3 * kD * 4;
   static constexpr int kOffBar = kOffKeep + kAttentionMaxTiles / 8;  // 2 mbarriers, TMEM base, fail flag
   static constexpr int kSmem = kOffBar + 64 + 1024;  // + alignment slack
   static constexpr int kVChunks = PV == 0 ? 8 : 4;   // 16-byte chunks per V / P row
@@ -103,6 +109,15 @@ __device__ __forceinline__ void unpack_chunk(const uint4& p, uint4& a, uint4& b)
   const uint32_t w[4] = {p.x ^ 0x88888888u, p.y ^ 0x88888888u, p.z ^ 0x88888888u, p.w ^ 0x88888888u};
   a = make_uint4(s8_from_nibbles(w[0]), s8_from_nibbles(w[0] >> 4), s8_from_nibbles(w[1]), s8_from_nibbles(w[1] >> 4));
   b = make_uint4(s8_from_nibbles(w[2]), s8_from_nibbles(w[2] >> 4), s8_from_nibbles(w[3]), s8_from_nibbles(w[3] >> 4));
+}
+
+// 2^x by the hardware approximation with subnormal results flushed to zero
+// (weights below 2^-126 of the row maximum; the reference's kernel rounds the
+// same values to subnormals, a difference far below the fp16 output's ulp).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -210,8 +225,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       sts128(sb + C::kOffK + buf * C::kKBytes + sw128_off(r, c + 1), hi);
     }
   };
-  auto issue_tile = [&](int tt, int buf) {
+  // Copies of tile tt into slot `slot`: K / V / k-scale buffers slot % 2, v-scales slot % 3.
+  auto issue_tile = [&](int tt, int slot) {
     const int k0 = tt * kTile;
+    const int buf = slot & 1;
     if constexpr (QK == 1) {
       for (int i = tid; i < kTile * 8; i += kThreads) {
         const int r = i >> 3, c = i & 7;
@@ -230,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     float* kss = reinterpret_cast<float*>(smem + C::kOffKs) + buf * kTile;
     if (tid < kTile) cp_async_4(kss + tid, ksg + (k0 + tid < Lk ? k0 + tid : 0), k0 + tid < Lk ? 4 : 0);
     if constexpr (PV == 1) {
-      float* vss = reinterpret_cast<float*>(smem + C::kOffVs) + buf * kD;
+      float* vss = reinterpret_cast<float*>(smem + C::kOffVs) + (slot % 3) * kD;
       cp_async_4(vss + tid, vsg + (size_t)tt * kD + tid, 4);
     }
     cp_async_commit();
@@ -242,35 +259,36 @@ __global__ void __launch_bounds__(kThreads, 2)
   float m = kNoScore, l = 0.0f;
 
   __syncthreads();  // keep bits visible
+  auto issue_s = [&](int slot) {  // S of the tile in slot `slot`: K buffer and S columns slot % 2
+    const uint64_t qd = tc::sw128_desc(sb + C::kOffQ);
+    const uint64_t kd = tc::sw128_desc(sb + C::kOffK + (slot & 1) * C::kKBytes);
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      umma_i8(tmem + kTmemS + 64 * (slot & 1), qd + (uint64_t)(2 * s), kd + (uint64_t)(2 * s),
+              idesc_i8(kTile, 1, 1), s > 0);
+    tc::umma_commit<1>(bar_s);
+  };
   int tcur = next_tile(-1);
-  if (tcur < n_tiles) issue_tile(tcur, 0);
   bool ok = true;
+  if (tcur < n_tiles) {
+    issue_tile(tcur, 0);
+    cp_async_wait_all();
+    if constexpr (QK == 2) store_k4(0);
+    fence_proxy_async();  // Q / K writes -> visible to the tensor core
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (tid == 0) issue_s(0);
+    __syncwarp();
+    const int t1 = next_tile(tcur);
+    if (t1 < n_tiles) issue_tile(t1, 1);
+  }
   uint32_t it = 0, oit = 0;
-  int buf = 0;
   while (tcur < n_tiles) {
     const int nvalid = Lk - tcur * kTile;  // keys of this tile inside Lk (>= 1)
     const int tnext = next_tile(tcur);
-    cp_async_wait_all();
-    if constexpr (QK == 2) store_k4(buf);
-    fence_proxy_async();  // Q / K / V / P writes of this thread -> visible to the tensor core
-    if (!ok) *s_fail = 1;
-    tc::tc_fence_before();
-    __syncthreads();  // tile tcur in buffer buf; the other buffer, S, O_t and P are free
-    tc::tc_fence_after();
-    if (*s_fail) break;
-    if (tnext < n_tiles) issue_tile(tnext, buf ^ 1);
-
-    // ---- S = Q K^T ----
-    if (tid == 0) {
-      const uint64_t qd = tc::sw128_desc(sb + C::kOffQ);
-      const uint64_t kd = tc::sw128_desc(sb + C::kOffK + buf * C::kKBytes);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        umma_i8(tmem + kTmemS, qd + (uint64_t)(2 * s), kd + (uint64_t)(2 * s), idesc_i8(kTile, 1, 1), s > 0);
-      tc::umma_commit<1>(bar_s);
-    }
-    __syncwarp();
-    ok = __all_sync(0xffffffffu, mbar_wait(bar_s, it & 1, kDevErrMmaBarrierTimeout));  // warp-uniform: tcgen05.ld
+    const int buf = it & 1;
+    ok = __all_sync(0xffffffffu, mbar_wait(bar_s, it & 1, kDevErrMmaBarrierTimeout)) && ok;  // warp-uniform
     tc::tc_fence_after();
 
     float p[kTile];
@@ -287,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       float tm[4] = {kNoScore, kNoScore, kNoScore, kNoScore};
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        tc::tmem_ld32(tmem + lane_addr + kTmemS + 32 * hf, sraw);
+        tc::tmem_ld32(tmem + lane_addr + kTmemS + 64 * buf + 32 * hf, sraw);
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 ks4 = *reinterpret_cast<const float4*>(kss + 32 * hf + j);
@@ -308,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const float tmax = fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3]));
       const float m_new = fmaxf(m, tmax);
-      const float alpha = exp2f(m - m_new);
+      const float alpha = ex2_ftz(m - m_new);
       m = m_new;
       if (alpha != 1.0f) {  // (x * 1 = x: skipping it changes nothing)
         l *= alpha;
@@ -316,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int i = 0; i < kD / 2; ++i) o[i] = __fmul2_rn(o[i], a2);
       }
-      const float rel = exp2f(tmax - m_new);
+      const float rel = ex2_ftz(tmax - m_new);
       float grel = rel;
 #pragma unroll
       for (int off = 1; off < 16; off <<= 1) grel = fmaxf(grel, __shfl_xor_sync(0xffffffffu, grel, off));
@@ -328,8 +346,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int key = 0; key < kTile; key += 2) {
         const float2 d = __fadd2_rn(make_float2(p[key], p[key + 1]), mm);
-        p[key] = exp2f(d.x);
-        p[key + 1] = exp2f(d.y);
+        p[key] = ex2_ftz(d.x);
+        p[key + 1] = ex2_ftz(d.y);
         ls = __fadd2_rn(ls, make_float2(p[key], p[key + 1]));
       }
       l += ls.x + ls.y;
@@ -371,16 +389,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-    fence_proxy_async();
+    // the next tile's copies (issued one tile ago) must have landed for S_{t+1}
+    cp_async_wait_all();
+    if constexpr (QK == 2) {
+      if (tnext < n_tiles) store_k4((it + 1) & 1);
+    }
+    fence_proxy_async();  // P, K writes of this thread -> visible to the tensor core
     if (!ok) *s_fail = 1;
     tc::tc_fence_before();
     const int any_run = __syncthreads_or(!skip);
     tc::tc_fence_after();
     if (*s_fail) break;
 
-    // ---- O_t = P V and the fold ----
-    if (any_run) {
-      if (tid == 0) {
+    // ---- S_{t+1} = Q K_{t+1}^T and O_t = P V_t ----
+    if (tid == 0) {
+      if (tnext < n_tiles) issue_s(it + 1);
+      if (any_run) {
         const uint64_t pd = tc::sw128_desc(sb + C::kOffP);
         const uint64_t vd = tc::sw128_desc(sb + C::kOffV + buf * C::kVBytes);
         if constexpr (PV == 1) {
@@ -394,12 +418,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc::umma_commit<1>(bar_o);
       }
-      __syncwarp();
+    }
+    __syncwarp();
+    if (any_run) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar_o, oit & 1, kDevErrMmaBarrierTimeout));
       ++oit;
       tc::tc_fence_after();
       if (ok) {  // the whole warp loads (tcgen05.ld is .sync.aligned); skipped half-warps do not fold
-        const float* vss = reinterpret_cast<const float*>(smem + C::kOffVs) + buf * kD;
+        const float* vss = reinterpret_cast<const float*>(smem + C::kOffVs) + (it % 3) * kD;
         // o = fma(rel/255 * v_scale, (float)acc - 128 sum(pq), o): 2^23 + acc
         // (acc < 2^23) minus 2^23 + 128 sum(pq) is that difference, exactly
         const float2 nb = make_float2(-(8388608.0f + 128.0f * pqsum), -(8388608.0f + 128.0f * pqsum));
@@ -428,13 +454,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
+    // tile t+2's copies: K / V / k-scale buffer `buf` (S_t and O_t are done), v-scales (it + 2) % 3
+    if (tnext < n_tiles) {
+      const int tnn = next_tile(tnext);
+      if (tnn < n_tiles) issue_tile(tnn, it + 2);
+    }
     tcur = tnext;
-    buf ^= 1;
     ++it;
   }
 
   cp_async_wait_all();
-  if (!ok) mirror_device_error(status_host);
+  if (!ok) {
+    mirror_device_error(status_host);
+    *s_fail = 1;
+  }
+  tc::tc_fence_before();
+  __syncthreads();  // every thread's failure flag is visible
+  tc::tc_fence_after();
   if (row_ok && !*s_fail) {
     __half* dst = out + ((size_t)b * Lq + row) * H * kD + (size_t)h * kD;
 #pragma unroll
