@@ -10,6 +10,7 @@ timed loop does not run out of L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --case qkv --m 1 [--reps 20] [--graph] [--copies 3]   (one GEMM shape, for ncu / quick timing)
+  python bench.py --attention-case int4/u8 [--tokens 4608] [--heads 24]  (one fused-attention shape)
 
 N = 1: the whole 4608-token sweep on one GPU. N > 1 (torchrun, one rank per
 GPU, NCCL): the same fixed workload split by token rows (rank r computes rows
@@ -701,6 +702,33 @@ def run_dit(args, world, rank, local):
         }))
 
 
+def run_attention_case(args):
+    """One fused-attention shape on cuda:0 (the command the attention ncu
+    summary under profiles/ profiles): batch 1, --heads heads, --tokens keys
+    and queries, seeded N(0, 1) fp16 q / k / v prepared once; prints the time
+    per call and TFLOP/s (4 * L^2 * 128 * heads)."""
+    from comfy_ui_gfx906_tools_b200 import attention as fa
+    qk, pv = args.attention_case.split("/")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, Hh = args.tokens, args.heads
+    g = torch.Generator(device=dev).manual_seed(77)
+    q, k, v = (torch.randn(1, Hh, L, 128, device=dev, dtype=torch.float16, generator=g) for _ in range(3))
+    prep = (*fa.prepare_qk(q, k, qk), *fa.prepare_v(v, pv))
+    for _ in range(2):
+        fa.attention_prepared(*prep, qk, pv, args.skip_below)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.reps):
+        fa.attention_prepared(*prep, qk, pv, args.skip_below)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.reps
+    print(json.dumps({"attention": f"{qk}/{pv}", "tokens": L, "heads": Hh, "ms": ms,
+                      "tflops": 4.0 * L * L * 128 * Hh / (ms * 1e-3) / 1e12, "skip_below": args.skip_below}))
+
+
 def run_case(args):
     """One GEMM shape on cuda:0, timed with CUDA events (the command the ncu
     summaries under profiles/ profile): synthetic Q4_0 weights used through
@@ -802,7 +830,16 @@ def main():
     ap.add_argument("--w4a4", action="store_true",
                     help="case: the integer-exact W4A4 GEMM (gemm_int4) on quantize_int4 activations")
     ap.add_argument("--int8", action="store_true", help="case: the int8 (W8A16) kernel, per-channel scales")
+    ap.add_argument("--attention-case", default=None,
+                    choices=[f"{a}/{b}" for a in ("fp16", "int8", "int4") for b in ("fp16", "u8")],
+                    help="time one fused-attention shape (with --tokens, --heads, --reps, --skip-below)")
+    ap.add_argument("--tokens", type=int, default=4608)
+    ap.add_argument("--heads", type=int, default=24)
+    ap.add_argument("--skip-below", type=float, default=0.0)
     args = ap.parse_args()
+    if args.attention_case is not None:
+        run_attention_case(args)
+        return
     if args.case is not None:
         run_case(args)
         return

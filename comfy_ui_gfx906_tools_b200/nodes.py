@@ -374,12 +374,14 @@ class Gfx906Int4UnetLoader:
 
 
 from .row_split import Gfx906RowSplitKrea2  # noqa: E402  (the multi-GPU split node, row_split.py)
+from .attention import Gfx906FusedAttention  # noqa: E402  (the fused attention node, attention.py)
 
 NODE_CLASS_MAPPINGS = {
     "Gfx906Int4Patch": Gfx906Int4Patch,
     "Gfx906Int4UnetLoader": Gfx906Int4UnetLoader,
     "Gfx906Int4Transcode": Gfx906Int4Transcode,
     "Gfx906RowSplitKrea2": Gfx906RowSplitKrea2,
+    "Gfx906FusedAttention": Gfx906FusedAttention,
 }
 
 NODE_DISPLAY_NAME_MAPPINGS = {
@@ -387,4 +389,5 @@ NODE_DISPLAY_NAME_MAPPINGS = {
     "Gfx906Int4Patch": "Gfx906 Int4 Quantize (test)",
     "Gfx906Int4UnetLoader": "Gfx906 Int4 UNet Loader (native kernel)",
     "Gfx906RowSplitKrea2": "Gfx906 Split Krea2 (2 GPUs)",
+    "Gfx906FusedAttention": "Gfx906 Fused Attention",
 }
