@@ -13,8 +13,9 @@ from comfy_ui_gfx906_tools_b200 import nodes, ops, synthetic
 def test_node_names_and_titles_match_reference():
     # nodes.py:602-622 for the nodes on the int4 DiT path
     assert set(nodes.NODE_CLASS_MAPPINGS) == {"Gfx906Int4Patch", "Gfx906Int4UnetLoader", "Gfx906Int4Transcode",
-                                              "Gfx906RowSplitKrea2"}
+                                              "Gfx906RowSplitKrea2", "Gfx906FusedAttention"}
     assert nodes.NODE_DISPLAY_NAME_MAPPINGS["Gfx906RowSplitKrea2"] == "Gfx906 Split Krea2 (2 GPUs)"
+    assert nodes.NODE_DISPLAY_NAME_MAPPINGS["Gfx906FusedAttention"] == "Gfx906 Fused Attention"
     assert nodes.NODE_DISPLAY_NAME_MAPPINGS["Gfx906Int4Transcode"] == "Gfx906 Int4 Transcode (native kernel, any source)"
     assert nodes.NODE_DISPLAY_NAME_MAPPINGS["Gfx906Int4Patch"] == "Gfx906 Int4 Quantize (test)"
     assert nodes.NODE_DISPLAY_NAME_MAPPINGS["Gfx906Int4UnetLoader"] == "Gfx906 Int4 UNet Loader (native kernel)"
