@@ -19,6 +19,8 @@ its outputs are bit-identical to the reference's on the same device:
 """
 from __future__ import annotations
 
+import logging
+
 import torch
 
 from . import _lib, ops
@@ -167,10 +169,12 @@ def _gqa_repeat(diffusion_model) -> int:
     return mod.heads // mod.kvheads if mod is not None else 1
 
 
-def make_override(qk: str, pv: str, skip_below: float, gqa_repeat: int = 1):
+def make_override(qk: str, pv: str, skip_below: float, gqa_repeat: int = 1, sparsity=None):
     """ComfyUI ``optimized_attention_override``: unmasked head-dim-128 calls
     with at least MIN_FUSED_TOKENS keys run the fused kernel, everything else
-    goes to ComfyUI's own backend (attention.py:101-132, dense only)."""
+    goes to ComfyUI's own backend (attention.py:101-132). ``sparsity`` (a
+    block_sparse.SparsityState) supplies keep masks while the key tiles fit the
+    kernel's mask limit."""
 
     def override(func, q, k, v, heads, mask=None, attn_precision=None, skip_reshape=False,
                  skip_output_reshape=False, **kwargs):
@@ -182,7 +186,10 @@ def make_override(qk: str, pv: str, skip_below: float, gqa_repeat: int = 1):
                         skip_output_reshape=skip_output_reshape, **kwargs)
         if gqa_repeat > 1 and k.shape[1] == q.shape[1]:
             k, v = k[:, ::gqa_repeat], v[:, ::gqa_repeat]
-        return fused_attention(q, k, v, qk, pv, skip_below).to(q.dtype)
+        keep = None
+        if sparsity is not None and -(-k.shape[2] // TILE) <= max_tiles():
+            keep = sparsity.keep(q, k, kwargs.get("transformer_options") or {})
+        return fused_attention(q, k, v, qk, pv, skip_below, keep).to(q.dtype)
 
     return override
 
@@ -190,10 +197,11 @@ def make_override(qk: str, pv: str, skip_below: float, gqa_repeat: int = 1):
 class Gfx906FusedAttention:
     """MODEL -> MODEL: routes the model's attention through the fused kernel
     (head dim 128, unmasked); other attention calls fall through to ComfyUI's
-    backend (attention.py:135-160). Block-sparse masks (sparse_tau > 0) are
-    accepted by the kernel through ``fused_attention(keep=...)``; the node's
-    online mask prediction and its calibration cache are not built here, so
-    the node runs dense and rejects sparse_tau > 0."""
+    backend (attention.py:135-160). sparse_tau > 0 runs block-sparse with
+    masks predicted per call and heads calibrated on the first call of each
+    sampling run (block_sparse.SparsityState); the reference's persistent
+    calibration cache is not built, so calibration="persistent" also
+    calibrates per run."""
 
     @classmethod
     def INPUT_TYPES(cls):
@@ -215,11 +223,15 @@ class Gfx906FusedAttention:
     TITLE = "Gfx906 Fused Attention"
 
     def patch(self, model, qk, pv, skip_below, sparse_tau=0.0, max_missed=0.02, calibration="persistent"):
-        if sparse_tau > 0:
-            raise NotImplementedError("Gfx906FusedAttention: block-sparse prediction (sparse_tau > 0) is not built; "
-                                      "pass keep masks to fused_attention directly")
+        from . import block_sparse
         diffusion_model = model.model.diffusion_model
+        sparsity = None
+        if sparse_tau > 0:
+            if calibration == "persistent":
+                logging.warning("[Gfx906 Attention] the persistent calibration cache is not built here; "
+                                "calibrating on the first step of every run")
+            sparsity = block_sparse.SparsityState(sparse_tau, max_missed, block_rows(qk))
         model = model.clone()
         model.model_options.setdefault("transformer_options", {})["optimized_attention_override"] = make_override(
-            qk, pv, skip_below, _gqa_repeat(diffusion_model))
+            qk, pv, skip_below, _gqa_repeat(diffusion_model), sparsity)
         return (model,)

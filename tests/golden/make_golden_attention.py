@@ -68,6 +68,20 @@ def main():
         vt, vs = att._prepare_v(v, mode)
         out[f"v_{mode}_vt"] = vt.numpy()
         out[f"v_{mode}_vs"] = vs.numpy()
+    # block-sparse prediction and calibration (block_sparse.py:60-90) on structured q / k:
+    # clustered keys so that the prediction keeps a strict subset of tiles
+    bs = sys.modules["ref_gfx906_pkg.block_sparse"]
+    # (runs of 64 keys / 32 queries around one of 6 centres, as neighbouring image tokens are alike)
+    centers = torch.randn(6, 128, generator=g) * 3
+    kid = torch.randint(0, 6, (1, 1, -(-450 // 64)), generator=g).repeat_interleave(64, -1)[..., :450]
+    qid = torch.randint(0, 6, (1, 2, -(-300 // 32)), generator=g).repeat_interleave(32, -1)[..., :300]
+    kc = centers[kid] + torch.randn(1, 1, 450, 128, generator=g) * 0.3
+    qc = centers[qid] + torch.randn(1, 2, 300, 128, generator=g) * 0.3
+    out["bs_q"], out["bs_k"] = qc.half().numpy(), kc.half().numpy()
+    for tau, rows in ((0.9, 128), (0.995, 64)):
+        keep = bs.predict_keep(qc.half(), kc.half(), tau, rows)
+        out[f"bs_keep_{rows}"] = keep.numpy()
+        out[f"bs_missed_{rows}"] = bs.missed_mass(qc.half(), kc.half(), keep, rows).numpy()
     path = os.path.join(HERE, "attention_prep.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")

@@ -125,3 +125,35 @@ def test_attention_rejects_bad_arguments(cuda):
         A.attention_prepared(qb, qs, kb, ks, vt, vs, "int8", "u8", 0.0, torch.ones(1, 4, 2, 1, dtype=torch.uint8,
                                                                                   device=cuda))
     assert A.block_rows("fp16") == 64 and A.block_rows("int4") == 128 and A.max_tiles() == 1024
+
+
+def test_override_block_sparse_end_to_end(cuda):
+    """The node's override with block-sparse masks (block_sparse.SparsityState):
+    the first call of a layer in a run is dense and calibrates, later calls
+    run the kernel with keep = prediction | dense heads; each equals
+    fused_attention with that mask, and the sparse output stays close to dense
+    (structured tokens: runs of 64 around a few centres)."""
+    from comfy_ui_gfx906_tools_b200 import block_sparse as BS
+    g = torch.Generator().manual_seed(9)
+    centers = torch.randn(6, 128, generator=g) * 3
+    L, H = 1024, 4
+    ids = torch.randint(0, 6, (1, H, L // 64), generator=g).repeat_interleave(64, -1)
+    q = (centers[ids] + torch.randn(1, H, L, 128, generator=g) * 0.3).half().to(cuda)
+    k = (centers[ids[:, :2]] + torch.randn(1, 2, L, 128, generator=g) * 0.3).half().to(cuda)
+    v = torch.randn(1, 2, L, 128, generator=g).half().to(cuda)
+    state = BS.SparsityState(0.995, 0.05, A.block_rows("int4"))
+    ov = A.make_override("int4", "u8", 0.0, 1, state)
+
+    def fallthrough(*a, **kw):
+        raise AssertionError("the override fell through to the host backend")
+
+    dense = ov(fallthrough, q, k, v, H, skip_reshape=True,
+               transformer_options={"block_index": 0, "sigmas": torch.tensor([1.0])})
+    assert torch.equal(dense, A.fused_attention(q, k, v, "int4", "u8"))
+    sparse = ov(fallthrough, q, k, v, H, skip_reshape=True,
+                transformer_options={"block_index": 0, "sigmas": torch.tensor([0.9])})
+    heads_ok = state.sparse_heads[(0, q.device, L, L)]
+    keep = (BS.predict_keep(q, k, 0.995, A.block_rows("int4")) | ~heads_ok[None, :, None, None]).to(torch.uint8)
+    assert torch.equal(sparse, A.fused_attention(q, k, v, "int4", "u8", 0.0, keep))
+    rel = ((sparse.float() - dense.float()).norm() / dense.float().norm()).item()
+    assert rel < 0.1, rel

@@ -132,5 +132,36 @@ def test_node_patch_installs_override():
     assert A._gqa_repeat(DM()) == 3
     (patched,) = A.Gfx906FusedAttention().patch(Model(), "int4", "u8", 1e-4, 0.0)
     assert callable(patched.model_options["transformer_options"]["optimized_attention_override"])
-    with pytest.raises(NotImplementedError, match="sparse_tau"):
-        A.Gfx906FusedAttention().patch(Model(), "int4", "u8", 1e-4, 0.5)
+    (sparse,) = A.Gfx906FusedAttention().patch(Model(), "int4", "u8", 1e-4, 0.5, 0.02, "per_run")
+    assert callable(sparse.model_options["transformer_options"]["optimized_attention_override"])
+
+
+# ---- block-sparse keep masks (block_sparse.py:60-90, 193-235 of the reference) ----
+from comfy_ui_gfx906_tools_b200 import block_sparse as BS  # noqa: E402
+
+
+@pytest.mark.parametrize("tau,rows", [(0.9, 128), (0.995, 64)])
+def test_predict_keep_and_missed_mass_are_the_references(gold, tau, rows):
+    q, k = torch.from_numpy(gold["bs_q"]), torch.from_numpy(gold["bs_k"])
+    keep = BS.predict_keep(q, k, tau, rows)
+    assert np.array_equal(keep.numpy(), gold[f"bs_keep_{rows}"])
+    assert 0 < keep.float().mean() < 1  # a strict subset: the fixture exercises the prediction
+    missed = BS.missed_mass(q, k, keep, rows)
+    assert np.allclose(missed.numpy(), gold[f"bs_missed_{rows}"], rtol=1e-5, atol=1e-7)
+
+
+def test_sparsity_state_calibrates_once_per_run():
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(1, 2, 300, 128, generator=g).half()
+    k = torch.randn(1, 1, 450, 128, generator=g).half()
+    st = BS.SparsityState(0.9, 1.0, 128)  # max_missed 1.0: every head may run sparse
+    opts = {"block_index": 3, "sigmas": torch.tensor([1.0])}
+    assert st.keep(q, k, {}) is None  # no block_index: dense
+    assert st.keep(q, k, opts) is None  # first call of the layer in this run: dense, calibrates
+    m = st.keep(q, k, {"block_index": 3, "sigmas": torch.tensor([0.5])})
+    assert m is not None and m.dtype == torch.uint8 and tuple(m.shape) == (1, 2, 3, 8)
+    assert torch.equal(m.bool(), BS.predict_keep(q, k, 0.9, 128))
+    assert st.keep(q, k, {"block_index": 3, "sigmas": torch.tensor([2.0])}) is None  # sigma rose: a new run
+    strict = BS.SparsityState(0.9, -1.0, 128)  # no head passes: dense masks everywhere
+    strict.keep(q, k, opts)
+    assert bool(strict.keep(q, k, opts).bool().all())
