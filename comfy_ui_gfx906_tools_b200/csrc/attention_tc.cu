@@ -316,14 +316,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           a = __fmul2_rn(__fmul2_rn(a, qsc2), make_float2(ks4.x, ks4.y));
           c = __fmul2_rn(__fmul2_rn(c, qsc2), make_float2(ks4.z, ks4.w));
           const int key = 32 * hf + j;
-          p[key] = key < nvalid ? a.x : kNoScore;
-          p[key + 1] = key + 1 < nvalid ? a.y : kNoScore;
-          p[key + 2] = key + 2 < nvalid ? c.x : kNoScore;
-          p[key + 3] = key + 3 < nvalid ? c.y : kNoScore;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) tm[e] = fmaxf(tm[e], p[key + e]);
+          p[key] = a.x;
+          p[key + 1] = a.y;
+          p[key + 2] = c.x;
+          p[key + 3] = c.y;
         }
       }
+      if (nvalid < kTile) {  // the last tile only (uniform over the CTA): keys past Lk score -1e30
+#pragma unroll
+        for (int key = 0; key < kTile; ++key)
+          if (key >= nvalid) p[key] = kNoScore;
+      }
+#pragma unroll
+      for (int key = 0; key < kTile; ++key) tm[key & 3] = fmaxf(tm[key & 3], p[key]);
       const float tmax = fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3]));
       const float m_new = fmaxf(m, tmax);
       const float alpha = ex2_ftz(m - m_new);
@@ -357,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // level = rint(p * 255 / rel): t + 2^23 rounds t (< 2^23) to the
         // nearest integer, ties to even, and leaves it in the low mantissa bits
         const float2 inv2 = make_float2(inv, inv);
-        const float2 k23 = make_float2(8388608.0f, 8388608.0f), km23 = make_float2(-8388608.0f, -8388608.0f);
-        float2 qs2 = make_float2(0.0f, 0.0f);
+        const float2 k23 = make_float2(8388608.0f, 8388608.0f);
+        uint32_t lsum = 0;  // sum of the levels, four bytes at a time
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[4];
@@ -367,15 +372,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int key = 16 * c + 4 * q;
             const float2 m01 = __fadd2_rn(__fmul2_rn(make_float2(p[key], p[key + 1]), inv2), k23);
             const float2 m23 = __fadd2_rn(__fmul2_rn(make_float2(p[key + 2], p[key + 3]), inv2), k23);
-            qs2 = __fadd2_rn(qs2, __fadd2_rn(m01, km23));
-            qs2 = __fadd2_rn(qs2, __fadd2_rn(m23, km23));
             const uint32_t x = prmt(__float_as_uint(m01.x), __float_as_uint(m01.y), 0x0040u);
             const uint32_t y = prmt(__float_as_uint(m23.x), __float_as_uint(m23.y), 0x0040u);
             w[q] = prmt(x, y, 0x5410u);
+            lsum = __dp4a(w[q], 0x01010101u, lsum);
           }
           sts128(prow + sw128_off(tid, c), make_uint4(w[0], w[1], w[2], w[3]));
         }
-        pqsum = qs2.x + qs2.y;  // integers < 2^24: exact
+        pqsum = (float)lsum;  // <= 64 * 255: exact
       } else {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
