@@ -120,6 +120,13 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
+// max(a, b, c): one three-input max (exact, like two two-input ones).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -328,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (key >= nvalid) p[key] = kNoScore;
       }
 #pragma unroll
-      for (int key = 0; key < kTile; ++key) tm[key & 3] = fmaxf(tm[key & 3], p[key]);
+      for (int key = 0; key < kTile; key += 2) tm[(key >> 1) & 3] = max3f(tm[(key >> 1) & 3], p[key], p[key + 1]);
       const float tmax = fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3]));
       const float m_new = fmaxf(m, tmax);
       const float alpha = ex2_ftz(m - m_new);
