@@ -486,8 +486,7 @@ def run_ours(args, world, rank, local):
             msa = time_steps(lambda: fa.attention_prepared(*prep, qk, pv, 1e-4), args.steps, args.warmup, world, dev,
                              stream) / args.steps
             attn["modes"][f"{qk}/{pv}"] = {"ms": msa, "value": flop_a / (msa * 1e-3) / 1e12,
-                                          "kernel": "attention_tc_kernel (tcgen05)" if qk != "fp16"
-                                          else "attention_kernel (mma.sync)"}
+                                          "kernel": "attention_tc_kernel (tcgen05)"}
             del prep
         mss = time_steps(lambda: torch.nn.functional.scaled_dot_product_attention(qa, ka, va), args.steps,
                          args.warmup, world, dev, stream) / args.steps

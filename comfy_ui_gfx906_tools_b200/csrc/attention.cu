@@ -451,7 +451,7 @@ int launch_attention(int qk_mode, int pv_mode, const void* q, const float* q_sca
                      const float* k_scale, const void* vt, const float* v_scale, const uint8_t* keep, void* out,
                      int B, int H, int KVH, int Lq, int Lk, float skip_below, cudaStream_t st) {
   if (B == 0 || H == 0 || Lq == 0) return GFX_OK;
-  if (attention_tc_selected(qk_mode))
+  if (attention_tc_selected(qk_mode, keep != nullptr))
     return launch_attention_tc(qk_mode, pv_mode, q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk,
                                skip_below, st);
 #define GFX_ATT_CASE(QKM, PVM)                                                                                    \

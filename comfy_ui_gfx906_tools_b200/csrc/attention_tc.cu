@@ -59,13 +59,19 @@ constexpr int kTmemO = 128;   // O_t: 128 columns
 
 template <int QK, int PV>
 struct Cfg {
-  static constexpr int kQBytes = kRows * 128;      // int8 Q tile, SW128
-  static constexpr int kKBytes = kTile * 128;      // int8 K tile, SW128
+  // int8 Q / K tiles: one SW128 tile [rows][128 B]; fp16: two, one per 64-element half of the
+  // head dimension. fp16 K is single-buffered (loaded once the previous S is done) so that two
+  // CTAs still fit on an SM.
+  static constexpr int kQHalf = kRows * 128;
+  static constexpr int kKHalf = kTile * 128;
+  static constexpr int kQBytes = QK == 0 ? 2 * kQHalf : kQHalf;
+  static constexpr int kKBytes = QK == 0 ? 2 * kKHalf : kKHalf;  // one buffer
+  static constexpr int kKBufs = QK == 0 ? 1 : 2;
   static constexpr int kVBytes = kD * 128;         // V tile: 128 channel rows of 128 B (u8 rows use half)
   static constexpr int kPBytes = kRows * 128;      // P tile
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;    // 2 buffers
-  static constexpr int kOffV = kOffK + 2 * kKBytes;  // 2 buffers
+  static constexpr int kOffV = kOffK + kKBufs * kKBytes;  // 2 buffers
   static constexpr int kOffP = kOffV + 2 * kVBytes;
   static constexpr int kOffKs = kOffP + kPBytes;   // 2 x 64 floats
   static constexpr int kOffVs = kOffKs + 2 * kTile * 4;  // 3 x 128 floats (the fold reads them one tile behind)
@@ -139,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                         const uint8_t* __restrict__ keep, __half* __restrict__ out, int H, int KVH, int Lq, int Lk,
                         int n_tiles, float skip_below, int* status_host) {
   using C = Cfg<QK, PV>;
-  constexpr int RB = QK == 1 ? 128 : 64;  // global Q / K row bytes
+  constexpr int RB = QK == 0 ? 256 : (QK == 1 ? 128 : 64);  // global Q / K row bytes
   constexpr int VROW = PV == 0 ? 128 : 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -187,16 +193,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
 
   // This thread's query row: lane t = 16 W + l holds the reference's row
-  // ty + 32 i of the block, ty = 4 W + (l & 3), i = l >> 2.
-  const int lrow = 4 * (tid >> 4) + (tid & 3) + 32 * ((tid & 15) >> 2);
+  // ty + TY i of its block, ty = 4 W + (l & 3), i = l >> 2 (int modes: one
+  // block of 128 rows, TY = 32; fp16: two blocks of 64 rows, TY = 16).
+  const int lrow = QK == 0 ? 64 * (tid >> 6) + 4 * ((tid & 63) >> 4) + (tid & 3) + 16 * ((tid & 15) >> 2)
+                           : 4 * (tid >> 4) + (tid & 3) + 32 * ((tid & 15) >> 2);
   const int row = qb * kRows + lrow;
   const bool row_ok = row < Lq;
-  const float qsc = row_ok ? q_scale[(size_t)(b * H + h) * Lq + row] : 1.0f;
+  const float qsc = (QK != 0 && row_ok) ? q_scale[(size_t)(b * H + h) * Lq + row] : 1.0f;
 
   // Q tile: this thread's row into SW128 row tid (int4: sign-extended).
   {
     const uint8_t* src = Qg + (size_t)(row_ok ? row : 0) * RB;
-    if constexpr (QK == 1) {
+    if constexpr (QK == 0) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        cp_async_16(smem + C::kOffQ + (c >> 3) * C::kQHalf + sw128_off(tid, c & 7), src + 16 * c, row_ok ? 16 : 0);
+    } else if constexpr (QK == 1) {
 #pragma unroll
       for (int c = 0; c < 8; ++c) cp_async_16(smem + C::kOffQ + sw128_off(tid, c), src + 16 * c, row_ok ? 16 : 0);
     } else {
@@ -232,11 +244,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       sts128(sb + C::kOffK + buf * C::kKBytes + sw128_off(r, c + 1), hi);
     }
   };
-  // Copies of tile tt into slot `slot`: K / V / k-scale buffers slot % 2, v-scales slot % 3.
-  auto issue_tile = [&](int tt, int slot) {
+  // fp16 K tile tt into the single K buffer (its two halves); committed with the next group.
+  auto load_k16 = [&](int tt) {
+    const int k0 = tt * kTile;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = tid + kThreads * j, r = i >> 4, c = i & 15;
+      const bool okr = k0 + r < Lk;
+      cp_async_16(smem + C::kOffK + (c >> 3) * C::kKHalf + sw128_off(r, c & 7),
+                  Kg + (size_t)(okr ? k0 + r : 0) * RB + 16 * c, okr ? 16 : 0);
+    }
+  };
+  // Copies of tile tt into slot `slot`: K / V / k-scale buffers slot % 2, v-scales slot % 3
+  // (fp16 K: only with with_k, into its single buffer).
+  auto issue_tile = [&](int tt, int slot, bool with_k) {
     const int k0 = tt * kTile;
     const int buf = slot & 1;
-    if constexpr (QK == 1) {
+    if constexpr (QK == 0) {
+      if (with_k) load_k16(tt);
+    } else if constexpr (QK == 1) {
       for (int i = tid; i < kTile * 8; i += kThreads) {
         const int r = i >> 3, c = i & 7;
         const bool ok = k0 + r < Lk;
@@ -251,8 +277,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int d = i / C::kVChunks, c = i % C::kVChunks;
       cp_async_16(smem + C::kOffV + buf * C::kVBytes + sw128_off(d, c), vsrc + (size_t)d * VROW + 16 * c, 16);
     }
-    float* kss = reinterpret_cast<float*>(smem + C::kOffKs) + buf * kTile;
-    if (tid < kTile) cp_async_4(kss + tid, ksg + (k0 + tid < Lk ? k0 + tid : 0), k0 + tid < Lk ? 4 : 0);
+    if constexpr (QK != 0) {
+      float* kss = reinterpret_cast<float*>(smem + C::kOffKs) + buf * kTile;
+      if (tid < kTile) cp_async_4(kss + tid, ksg + (k0 + tid < Lk ? k0 + tid : 0), k0 + tid < Lk ? 4 : 0);
+    }
     if constexpr (PV == 1) {
       float* vss = reinterpret_cast<float*>(smem + C::kOffVs) + (slot % 3) * kD;
       cp_async_4(vss + tid, vsg + (size_t)tt * kD + tid, 4);
@@ -267,18 +295,28 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   __syncthreads();  // keep bits visible
   auto issue_s = [&](int slot) {  // S of the tile in slot `slot`: K buffer and S columns slot % 2
-    const uint64_t qd = tc::sw128_desc(sb + C::kOffQ);
-    const uint64_t kd = tc::sw128_desc(sb + C::kOffK + (slot & 1) * C::kKBytes);
+    if constexpr (QK == 0) {  // fp16: 8 x K = 16, two 64-element halves of the head dimension
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-      umma_i8(tmem + kTmemS + 64 * (slot & 1), qd + (uint64_t)(2 * s), kd + (uint64_t)(2 * s),
-              idesc_i8(kTile, 1, 1), s > 0);
+      for (int s = 0; s < 8; ++s) {
+        const uint64_t qd = tc::sw128_desc(sb + C::kOffQ + (s >> 2) * C::kQHalf);
+        const uint64_t kd = tc::sw128_desc(sb + C::kOffK + (s >> 2) * C::kKHalf);
+        tc::umma_f16<1>(tmem + kTmemS + 64 * (slot & 1), qd + (uint64_t)(2 * (s & 3)), kd + (uint64_t)(2 * (s & 3)),
+                        idesc_f16(kTile), s > 0);
+      }
+    } else {
+      const uint64_t qd = tc::sw128_desc(sb + C::kOffQ);
+      const uint64_t kd = tc::sw128_desc(sb + C::kOffK + (slot & 1) * C::kKBytes);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        umma_i8(tmem + kTmemS + 64 * (slot & 1), qd + (uint64_t)(2 * s), kd + (uint64_t)(2 * s),
+                idesc_i8(kTile, 1, 1), s > 0);
+    }
     tc::umma_commit<1>(bar_s);
   };
   int tcur = next_tile(-1);
   bool ok = true;
   if (tcur < n_tiles) {
-    issue_tile(tcur, 0);
+    issue_tile(tcur, 0, true);
     cp_async_wait_all();
     if constexpr (QK == 2) store_k4(0);
     fence_proxy_async();  // Q / K writes -> visible to the tensor core
@@ -288,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (tid == 0) issue_s(0);
     __syncwarp();
     const int t1 = next_tile(tcur);
-    if (t1 < n_tiles) issue_tile(t1, 1);
+    if (t1 < n_tiles) issue_tile(t1, 1, false);
   }
   uint32_t it = 0, oit = 0;
   while (tcur < n_tiles) {
@@ -297,6 +335,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int buf = it & 1;
     ok = __all_sync(0xffffffffu, mbar_wait(bar_s, it & 1, kDevErrMmaBarrierTimeout)) && ok;  // warp-uniform
     tc::tc_fence_after();
+    if constexpr (QK == 0) {  // S_t is done with the single fp16 K buffer: bring in K_{t+1}
+      if (tnext < n_tiles && ok) {
+        load_k16(tnext);
+        cp_async_commit();
+      }
+    }
 
     float p[kTile];
     bool skip = true;
@@ -313,6 +357,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         tc::tmem_ld32(tmem + lane_addr + kTmemS + 64 * buf + 32 * hf, sraw);
+        if constexpr (QK == 0) {  // fp16 Q.K: the fp32 dot is the score (the scale is folded into Q)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) p[32 * hf + j] = __uint_as_float(sraw[j]);
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 ks4 = *reinterpret_cast<const float4*>(kss + 32 * hf + j);
@@ -468,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // tile t+2's copies: K / V / k-scale buffer `buf` (S_t and O_t are done), v-scales (it + 2) % 3
     if (tnext < n_tiles) {
       const int tnn = next_tile(tnext);
-      if (tnn < n_tiles) issue_tile(tnn, it + 2);
+      if (tnn < n_tiles) issue_tile(tnn, it + 2, false);
     }
     tcur = tnext;
     ++it;
@@ -526,10 +575,12 @@ static int launch(const void* q, const float* qs, const void* k, const float* ks
 
 }  // namespace attn_tc
 
-// The tensor-core kernel for the int Q.K modes unless GFX906_B200_ATTN_MMA_SYNC
-// is set to a nonzero value (then the mma.sync kernel of attention.cu runs).
-bool attention_tc_selected(int qk_mode) {
-  if (qk_mode != 1 && qk_mode != 2) return false;
+// The tensor-core kernel for every mode (fp16 Q.K without a keep mask) unless
+// GFX906_B200_ATTN_MMA_SYNC is set to a nonzero value (then the mma.sync kernel
+// of attention.cu runs).
+bool attention_tc_selected(int qk_mode, bool keep) {
+  // fp16 Q.K keep masks come in 64-row blocks, half of this kernel's 128-row CTA
+  if (qk_mode == 0 && keep) return false;
   const char* e = getenv("GFX906_B200_ATTN_MMA_SYNC");
   return !(e && atoi(e) != 0);
 }
@@ -538,6 +589,10 @@ int launch_attention_tc(int qk_mode, int pv_mode, const void* q, const float* q_
                         const float* k_scale, const void* vt, const float* v_scale, const uint8_t* keep, void* out,
                         int B, int H, int KVH, int Lq, int Lk, float skip_below, cudaStream_t st) {
   if (B == 0 || H == 0 || Lq == 0) return GFX_OK;
+  if (qk_mode == 0 && pv_mode == 0)
+    return attn_tc::launch<0, 0>(q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk, skip_below, st);
+  if (qk_mode == 0 && pv_mode == 1)
+    return attn_tc::launch<0, 1>(q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk, skip_below, st);
   if (qk_mode == 1 && pv_mode == 0)
     return attn_tc::launch<1, 0>(q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk, skip_below, st);
   if (qk_mode == 1 && pv_mode == 1)
@@ -546,7 +601,7 @@ int launch_attention_tc(int qk_mode, int pv_mode, const void* q, const float* q_
     return attn_tc::launch<2, 0>(q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk, skip_below, st);
   if (qk_mode == 2 && pv_mode == 1)
     return attn_tc::launch<2, 1>(q, q_scale, k, k_scale, vt, v_scale, keep, out, B, H, KVH, Lq, Lk, skip_below, st);
-  return set_error(GFX_ERR_INVALID, "attention: the tensor-core kernel takes the int Q.K modes, got qk=%d", qk_mode);
+  return set_error(GFX_ERR_INVALID, "attention: bad modes qk=%d pv=%d", qk_mode, pv_mode);
 }
 
 }  // namespace gfx

@@ -80,8 +80,8 @@ int launch_quantize_int4_cols(const void* x, long long row_stride, int R, int C,
 // qk_mode 0 fp16 / 1 int8 / 2 int4, pv_mode 0 fp16 / 1 u8; layouts as the C ABI's attention().
 constexpr int kAttentionMaxTiles = 1024;  // key tiles a keep mask may cover (65536 keys)
 int attention_rows_per_block(int qk_mode);
-// tcgen05 kernel for the int Q.K modes -- attention_tc.cu (launch_attention routes to it when selected)
-bool attention_tc_selected(int qk_mode);
+// tcgen05 kernel -- attention_tc.cu (launch_attention routes to it when selected)
+bool attention_tc_selected(int qk_mode, bool keep);
 int launch_attention_tc(int qk_mode, int pv_mode, const void* q, const float* q_scale, const void* k,
                         const float* k_scale, const void* vt, const float* v_scale, const uint8_t* keep, void* out,
                         int B, int H, int KVH, int Lq, int Lk, float skip_below, cudaStream_t stream);

@@ -1,4 +1,4 @@
-"""Fused attention kernel (C ABI ``attention``, csrc/attention.cu) against the
+"""Fused attention kernels (C ABI ``attention``: csrc/attention_tc.cu, csrc/attention.cu) against the
 oracle's restatement of the reference kernel (oracle/attention.py, after
 nodes/ComfyUI-Gfx906Int4/csrc/attention.hip:83-357) on the same prepared
 inputs, and end to end (``fused_attention``) against exact attention.
@@ -56,18 +56,19 @@ def test_kernel_equals_oracle(cuda, qk, pv, B, H, KVH, Lq, Lk):
     _close(*_both(q, k, v, qk, pv))
 
 
-@pytest.mark.parametrize("qk,pv", [m for m in MODES if m[0] != "fp16"])
+@pytest.mark.parametrize("qk,pv", MODES)
 @pytest.mark.parametrize("B,H,KVH,Lq,Lk", [(1, 8, 2, 300, 300), (2, 4, 4, 130, 333)])
 def test_mma_sync_kernel_equals_oracle(cuda, monkeypatch, qk, pv, B, H, KVH, Lq, Lk):
-    """The int Q.K modes run on the tcgen05 kernel (csrc/attention_tc.cu) by
-    default; GFX906_B200_ATTN_MMA_SYNC=1 selects the mma.sync kernel
-    (csrc/attention.cu), which must agree with the oracle as well."""
+    """Every mode runs on the tcgen05 kernel (csrc/attention_tc.cu) by default
+    (fp16 Q.K with a keep mask on the mma.sync kernel); GFX906_B200_ATTN_MMA_SYNC=1
+    selects the mma.sync kernel (csrc/attention.cu) for all, which must agree
+    with the oracle as well."""
     monkeypatch.setenv("GFX906_B200_ATTN_MMA_SYNC", "1")
     q, k, v = _inputs(B, H, KVH, Lq, Lk, 31 + Lq + Lk + H, cuda)
     _close(*_both(q, k, v, qk, pv))
 
 
-@pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "u8"), ("fp16", "fp16")])
+@pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "u8"), ("fp16", "fp16"), ("fp16", "u8")])
 def test_kernel_keep_mask_equals_oracle(cuda, qk, pv):
     B, H, KVH, L = 1, 4, 2, 700
     q, k, v = _inputs(B, H, KVH, L, L, 5, cuda)
@@ -80,7 +81,7 @@ def test_kernel_keep_mask_equals_oracle(cuda, qk, pv):
     _close(*_both(q, k, v, qk, pv, keep=keep.to(cuda)))
 
 
-@pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "fp16"), ("fp16", "u8")])
+@pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "fp16"), ("fp16", "u8"), ("fp16", "fp16")])
 def test_kernel_skip_below_equals_oracle(cuda, qk, pv):
     """skip_below drops a key tile's P.V per warp of 16 rows, the rows of one
     wave of the reference kernel; with peaked scores many tiles skip."""
