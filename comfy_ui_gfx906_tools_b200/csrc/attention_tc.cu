@@ -1,5 +1,6 @@
-// Fused quantized attention on the 5th-generation tensor cores, int8 / int4
-// Q.K (the reference's default modes): the arithmetic of attention_kernel
+// Fused quantized attention on the 5th-generation tensor cores, every Q.K /
+// P.V mode (fp16 Q.K with a keep mask excepted: its mask blocks are 64 rows,
+// half a CTA here; attention.cu runs it): the arithmetic of attention_kernel
 // (nodes/ComfyUI-Gfx906Int4/csrc/attention.hip:83-357) as restated in
 // attention.cu, with both products as tcgen05.mma and one thread per query
 // row.
@@ -10,7 +11,9 @@
 // 64-key tile:
 //   S  = Q K^T     tcgen05.mma.kind::i8 (s8 x s8 -> s32), M 128, N 64, K 4 x 32;
 //                  Q (int8, or int4 codes sign-extended once) and K in shared
-//                  memory, SWIZZLE_128B K-major, S in TMEM columns [0, 64)
+//                  memory, SWIZZLE_128B K-major; fp16 Q.K: kind::f16, K 8 x 16
+//                  over two SWIZZLE_128B halves of the head dimension (rows
+//                  grouped in the reference's 64-row fp16 blocks)
 //   softmax        each thread loads its row of S (tcgen05.ld), scales,
 //                  masks, updates m / l / alpha, decides the skip with its
 //                  half-warp, writes its row of P (u8 levels or fp16) to shared
