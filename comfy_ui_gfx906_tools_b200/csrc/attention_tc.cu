@@ -1,6 +1,6 @@
 // Fused quantized attention on the 5th-generation tensor cores, every Q.K /
-// P.V mode (fp16 Q.K with a keep mask excepted: its mask blocks are 64 rows,
-// half a CTA here; attention.cu runs it): the arithmetic of attention_kernel
+// P.V mode (fp16 Q.K keep masks come in 64-row blocks: a CTA visits the union
+// of its two blocks' tiles and each warp only its own block's): the arithmetic of attention_kernel
 // (nodes/ComfyUI-Gfx906Int4/csrc/attention.hip:83-357) as restated in
 // attention.cu, with both products as tcgen05.mma and one thread per query
 // row.
@@ -79,7 +79,7 @@ struct Cfg {
   static constexpr int kOffKs = kOffP + kPBytes;   // 2 x 64 floats
   static constexpr int kOffVs = kOffKs + 2 * kTile * 4;  // 3 x 128 floats (the fold reads them one tile behind)
   static constexpr int kOffKeep = kOffVs + 3 * kD * 4;
-  static constexpr int kOffBar = kOffKeep + kAttentionMaxTiles / 8;  // 2 mbarriers, TMEM base, fail flag
+  static constexpr int kOffBar = kOffKeep + 2 * kAttentionMaxTiles / 8;  // 2 mbarriers, TMEM base, fail flag
   static constexpr int kSmem = kOffBar + 64 + 1024;  // + alignment slack
   static constexpr int kVChunks = PV == 0 ? 8 : 4;   // 16-byte chunks per V / P row
 };
@@ -174,12 +174,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     *s_fail = 0;
     fence_barrier_init();
   }
+  // keep bits: one mask block per CTA (int modes: 128 rows), or two (fp16 Q.K: blocks of 64
+  // rows, the second at keep_s + kAttentionMaxTiles / 8, all clear past the last block)
+  constexpr int kMaskBlocks = QK == 0 ? 2 : 1;
   if (keep) {
-    const uint8_t* kg = keep + ((size_t)(b * H + h) * gridDim.x + qb) * n_tiles;
-    for (int i = tid; i < (n_tiles + 7) / 8; i += kThreads) {
-      uint32_t bits = 0;
-      for (int j = 0; j < 8 && i * 8 + j < n_tiles; ++j) bits |= (uint32_t)(kg[i * 8 + j] != 0) << j;
-      keep_s[i] = (uint8_t)bits;
+    const int n_qb = QK == 0 ? (Lq + 63) / 64 : (int)gridDim.x;
+    for (int mb = 0; mb < kMaskBlocks; ++mb) {
+      const int blk = kMaskBlocks * qb + mb;
+      const uint8_t* kg = keep + ((size_t)(b * H + h) * n_qb + blk) * n_tiles;
+      for (int i = tid; i < (n_tiles + 7) / 8; i += kThreads) {
+        uint32_t bits = 0;
+        for (int j = 0; j < 8 && i * 8 + j < n_tiles && blk < n_qb; ++j) bits |= (uint32_t)(kg[i * 8 + j] != 0) << j;
+        keep_s[mb * (kAttentionMaxTiles / 8) + i] = (uint8_t)bits;
+      }
     }
   }
   if (warp == 0) tc::tmem_alloc<1>(tmem_slot, kTmemCols);
@@ -189,11 +196,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_addr = (uint32_t)(32 * warp) << 16;
 
+  // a tile is visited when any of the CTA's mask blocks keeps it; this thread's rows take part
+  // when its own block does (fp16: warps 0-1 hold block 0, warps 2-3 block 1: warp-uniform)
+  auto kept = [&](int mb, int tt) { return (keep_s[mb * (kAttentionMaxTiles / 8) + (tt >> 3)] >> (tt & 7)) & 1; };
   auto next_tile = [&](int tt) {
     ++tt;
-    while (keep && tt < n_tiles && !((keep_s[tt >> 3] >> (tt & 7)) & 1)) ++tt;
+    while (keep && tt < n_tiles && !(kept(0, tt) || (kMaskBlocks == 2 && kept(1, tt)))) ++tt;
     return tt;
   };
+  const int my_block = QK == 0 ? (tid >> 6) : 0;
 
   // This thread's query row: lane t = 16 W + l holds the reference's row
   // ty + TY i of its block, ty = 4 W + (l & 3), i = l >> 2 (int modes: one
@@ -348,7 +359,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     float p[kTile];
     bool skip = true;
     float pscale = 0.0f, pqsum = 0.0f;
-    if (ok) {
+    // rows whose mask block does not keep this tile leave it out entirely (m, l, o unchanged,
+    // no fold), as the reference's block that never visits it
+    const bool visit = !keep || kept(my_block, tcur);
+    if (ok && visit) {
       // scores: ((float)dot * q_scale) * k_scale, each product rounded as the
       // reference; |dot| <= 128^3 < 2^22, so 1.5 * 2^23 + dot is exact and
       // its float bits minus 1.5 * 2^23 give (float)dot without a conversion
@@ -363,8 +377,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if constexpr (QK == 0) {  // fp16 Q.K: the fp32 dot is the score (the scale is folded into Q)
 #pragma unroll
           for (int j = 0; j < 32; ++j) p[32 * hf + j] = __uint_as_float(sraw[j]);
-          continue;
-        }
+        } else {
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 ks4 = *reinterpret_cast<const float4*>(kss + 32 * hf + j);
@@ -379,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           p[key + 1] = a.y;
           p[key + 2] = c.x;
           p[key + 3] = c.y;
+        }
         }
       }
       if (nvalid < kTile) {  // the last tile only (uniform over the CTA): keys past Lk score -1e30
@@ -578,12 +592,11 @@ static int launch(const void* q, const float* qs, const void* k, const float* ks
 
 }  // namespace attn_tc
 
-// The tensor-core kernel for every mode (fp16 Q.K without a keep mask) unless
-// GFX906_B200_ATTN_MMA_SYNC is set to a nonzero value (then the mma.sync kernel
-// of attention.cu runs).
+// The tensor-core kernel for every mode unless GFX906_B200_ATTN_MMA_SYNC is set
+// to a nonzero value (then the mma.sync kernel of attention.cu runs).
 bool attention_tc_selected(int qk_mode, bool keep) {
-  // fp16 Q.K keep masks come in 64-row blocks, half of this kernel's 128-row CTA
-  if (qk_mode == 0 && keep) return false;
+  (void)qk_mode;
+  (void)keep;
   const char* e = getenv("GFX906_B200_ATTN_MMA_SYNC");
   return !(e && atoi(e) != 0);
 }

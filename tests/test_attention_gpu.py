@@ -68,8 +68,13 @@ def test_mma_sync_kernel_equals_oracle(cuda, monkeypatch, qk, pv, B, H, KVH, Lq,
     _close(*_both(q, k, v, qk, pv))
 
 
+@pytest.mark.parametrize("impl", ["tcgen05", "mma.sync"])
 @pytest.mark.parametrize("qk,pv", [("int8", "u8"), ("int4", "u8"), ("fp16", "fp16"), ("fp16", "u8")])
-def test_kernel_keep_mask_equals_oracle(cuda, qk, pv):
+def test_kernel_keep_mask_equals_oracle(cuda, monkeypatch, impl, qk, pv):
+    """Keep masks per (query block, key tile): the fp16 modes' blocks are 64 rows,
+    so one tcgen05 CTA of 128 rows visits the union of two blocks' tiles and each
+    warp only its own block's."""
+    monkeypatch.setenv("GFX906_B200_ATTN_MMA_SYNC", "1" if impl == "mma.sync" else "0")
     B, H, KVH, L = 1, 4, 2, 700
     q, k, v = _inputs(B, H, KVH, L, L, 5, cuda)
     rows, tiles = A.block_rows(qk), -(-L // 64)
