@@ -95,8 +95,8 @@ def max_tiles() -> int:
     return _lib.load().attention_max_tiles()
 
 
-def attention_prepared(qb, qs, kb, ks, vt, vs, qk: str, pv: str, skip_below: float = 0.0, keep=None,
-                       heads: int | None = None) -> torch.Tensor:
+def attention_prepared(qb, qs, kb, ks, vt, vs, qk: str, pv: str, skip_below: float = 0.0,
+                       keep=None) -> torch.Tensor:
     """The kernel on prepared inputs (the binding's ``attention``,
     binding.cpp:114-170): Q [B, H, Lq, qrow] / K [B, KVH, Lk, qrow] uint8,
     scales fp32, Vt [B, KVH, tiles, 128, 64 * vbytes] uint8 -> fp16 [B, Lq, H * 128]."""
