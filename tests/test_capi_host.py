@@ -120,3 +120,24 @@ def test_allgather_and_peer_barrier_argument_checks(built_lib):
     assert built_lib.gfx_peer_barrier(ctypes.cast(ptrs, ctypes.c_void_p), 2, -1, None) == _lib.GFX_ERR_INVALID
     assert built_lib.gfx_peer_barrier(ctypes.cast(nulls, ctypes.c_void_p), 2, 0, None) == _lib.GFX_ERR_INVALID
     assert "rank 1 is null" in _lib.last_error()
+
+
+def test_attention_argument_checks(built_lib):
+    # argument checks only: nothing is launched (the addresses are 16-byte aligned stand-ins, never read)
+    P = 4096
+
+    def att(qk=1, pv=1, q=P, qs=P, k=P, ks=P, vt=P, vs=P, keep=None, out=P, B=1, H=4, KVH=2, Lq=64, Lk=64):
+        return built_lib.attention(qk, pv, q, qs, k, ks, vt, vs, keep, out, B, H, KVH, Lq, Lk, 0.0, None)
+
+    assert att(qk=3) == _lib.GFX_ERR_INVALID and "qk_mode" in _lib.last_error()
+    assert att(pv=2) == _lib.GFX_ERR_INVALID and "pv_mode" in _lib.last_error()
+    assert att(H=3) == _lib.GFX_ERR_INVALID and "multiple of KVH" in _lib.last_error()
+    assert att(Lk=0) == _lib.GFX_ERR_INVALID
+    assert att(qs=None) == _lib.GFX_ERR_INVALID and "q_scale" in _lib.last_error()
+    assert att(qk=0, qs=None, ks=None, vs=None) == _lib.GFX_ERR_INVALID and "v_scale" in _lib.last_error()
+    assert att(q=P + 8) == _lib.GFX_ERR_INVALID and "16-byte" in _lib.last_error()
+    assert att(keep=P, Lk=64 * 1025) == _lib.GFX_ERR_INVALID and "key tiles" in _lib.last_error()
+    assert att(qk=0, qs=None, ks=None, pv=0, vs=None, B=0) == _lib.GFX_OK  # nothing to compute
+    assert built_lib.attention_block_rows(0) == 64 and built_lib.attention_block_rows(2) == 128
+    assert built_lib.attention_block_rows(5) == -1
+    assert built_lib.attention_max_tiles() == 1024
