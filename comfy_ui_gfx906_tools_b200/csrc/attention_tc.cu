@@ -129,6 +129,18 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
+// 32 columns of this warp's 32 TMEM lanes, without waiting (tc::tmem_wait_ld waits for all).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 // max(a, b, c): one three-input max (exact, like two two-input ones).
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
@@ -508,12 +520,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float2 nb = make_float2(-(8388608.0f + 128.0f * pqsum), -(8388608.0f + 128.0f * pqsum));
         const float2 ps2 = make_float2(pscale, pscale);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t raw[32];
-          tc::tmem_ld32(tmem + lane_addr + kTmemO + 32 * cc, raw);
+        for (int cp = 0; cp < 4; cp += 2) {
+          uint32_t rw[2][32];  // two 32-column chunks in flight, one wait
+          tmem_ld32_nowait(tmem + lane_addr + kTmemO + 32 * cp, rw[0]);
+          tmem_ld32_nowait(tmem + lane_addr + kTmemO + 32 * cp + 32, rw[1]);
+          tc::tmem_wait_ld();
           if (skip) continue;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
+          for (int jj = 0; jj < 64; jj += 4) {
+          const int cc = cp + (jj >> 5), j = jj & 31;
+          const uint32_t* raw = rw[jj >> 5];
+          {
             const int i = 16 * cc + j / 2;  // channel pair index
             if constexpr (PV == 1) {
               const float4 v4 = *reinterpret_cast<const float4*>(vss + 32 * cc + j);
@@ -527,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               o[i] = __fadd2_rn(o[i], make_float2(__uint_as_float(raw[j]), __uint_as_float(raw[j + 1])));
               o[i + 1] = __fadd2_rn(o[i + 1], make_float2(__uint_as_float(raw[j + 2]), __uint_as_float(raw[j + 3])));
             }
+          }
           }
         }
       }
